@@ -1,0 +1,110 @@
+"""ctypes binding of libeva_moe.so (the C ABI declared in include/eva_moe.h).
+
+There is no fallback: if the library is missing or fails to load, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+from .config import MoEConfig
+
+LIB_PATH = Path(__file__).resolve().parent / "libeva_moe.so"
+
+EVA_OK, EVA_ERR_INVALID, EVA_ERR_CUDA, EVA_ERR_WORKSPACE = 0, 1, 2, 3
+STATUS_BAD_EXPERT, STATUS_TIMEOUT, STATUS_CAPACITY = 1, 2, 4
+ACT_CLAMP_AFTER, ACT_CLAMP_BEFORE = 0, 1
+
+# every symbol include/eva_moe.h declares
+EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_status", "eva_moe_route",
+           "eva_moe_topk", "eva_moe_permute", "eva_moe_experts", "eva_moe_forward", "eva_exl3_dequant",
+           "eva_moe_arch")
+
+
+class EvaMoeShape(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int32), ("inter", ctypes.c_int32), ("n_experts", ctypes.c_int32),
+                ("topk", ctypes.c_int32), ("bits", ctypes.c_int32), ("shared_inter", ctypes.c_int32),
+                ("shared_bits", ctypes.c_int32), ("router", ctypes.c_int32), ("n_group", ctypes.c_int32),
+                ("topk_group", ctypes.c_int32), ("norm_topk", ctypes.c_int32), ("act_routed", ctypes.c_int32),
+                ("act_shared", ctypes.c_int32), ("route_scale", ctypes.c_float), ("swiglu_limit", ctypes.c_float)]
+
+
+def shape_of(cfg: MoEConfig, *, shared: bool = True, bits: int | None = None, limit: float | None = None,
+             act_routed: int = ACT_CLAMP_AFTER, act_shared: int = ACT_CLAMP_BEFORE,
+             n_experts: int | None = None) -> EvaMoeShape:
+    return EvaMoeShape(cfg.hidden, cfg.inter, cfg.n_experts if n_experts is None else n_experts, cfg.topk,
+                       cfg.bits if bits is None else bits, cfg.shared_inter if shared else 0, cfg.shared_bits,
+                       cfg.router_code, cfg.n_group, cfg.topk_group, int(cfg.norm_topk), act_routed, act_shared,
+                       float(cfg.route_scale), float(cfg.swiglu_limit if limit is None else limit))
+
+
+_lib = None
+
+
+def load(build_if_missing: bool = True):
+    """Load libeva_moe.so (building it with nvcc first when it is missing and nvcc exists)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists() and build_if_missing and not os.environ.get("EVA_NO_BUILD"):
+        from .build import build
+        build()
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"libeva_moe.so not found at {LIB_PATH}; run `python -m eva_b200.build`")
+    L = ctypes.CDLL(str(LIB_PATH))
+    vp, i32, sz, P = ctypes.c_void_p, ctypes.c_int32, ctypes.c_size_t, ctypes.POINTER
+    shp = P(EvaMoeShape)
+    L.eva_moe_workspace_bytes.restype = sz
+    L.eva_moe_workspace_bytes.argtypes = [shp, i32]
+    L.eva_moe_clear_status.restype = ctypes.c_int
+    L.eva_moe_clear_status.argtypes = [vp, vp]
+    L.eva_moe_read_status.restype = ctypes.c_int
+    L.eva_moe_read_status.argtypes = [vp, P(i32), vp]
+    L.eva_moe_route.restype = ctypes.c_int
+    L.eva_moe_route.argtypes = [shp, vp, i32, i32, vp, vp, vp, vp, vp, vp, sz, vp]
+    L.eva_moe_topk.restype = ctypes.c_int
+    L.eva_moe_topk.argtypes = [shp, vp, i32, vp, vp, vp, vp]
+    L.eva_moe_permute.restype = ctypes.c_int
+    L.eva_moe_permute.argtypes = [shp, vp, i32, vp, i32, i32, vp, vp, vp]
+    L.eva_moe_experts.restype = ctypes.c_int
+    L.eva_moe_experts.argtypes = [shp, vp, i32, i32, vp, i32, vp, P(vp), P(ctypes.c_int64), vp, sz, vp, vp, vp]
+    L.eva_moe_forward.restype = ctypes.c_int
+    L.eva_moe_forward.argtypes = [shp, vp, i32, i32, vp, vp, P(vp), P(ctypes.c_int64), vp, sz, vp, vp,
+                                  vp, vp, vp, vp]
+    L.eva_exl3_dequant.restype = ctypes.c_int
+    L.eva_exl3_dequant.argtypes = [vp, i32, i32, i32, vp, vp]
+    L.eva_moe_arch.restype = i32
+    L.eva_moe_arch.argtypes = []
+    _lib = L
+    return L
+
+
+def check(rc: int, what: str) -> None:
+    if rc == EVA_OK:
+        return
+    if rc == EVA_ERR_INVALID:
+        raise ValueError(f"{what}: invalid argument (shape, pointer, alignment or unsupported K)")
+    if rc == EVA_ERR_WORKSPACE:
+        raise ValueError(f"{what}: workspace too small")
+    raise RuntimeError(f"{what}: CUDA launch failed (rc={rc})")
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def table_array(tables) -> ctypes.Array:
+    arr = (ctypes.c_void_p * 9)()
+    for i, t in enumerate(tables):
+        arr[i] = t.data_ptr() if hasattr(t, "data_ptr") else int(t)
+    return arr
+
+
+def shared_array(addrs) -> ctypes.Array | None:
+    if addrs is None:
+        return None
+    arr = (ctypes.c_int64 * 9)()
+    for i, a in enumerate(addrs):
+        arr[i] = int(a)
+    return arr

@@ -1,0 +1,265 @@
+// extern "C" entry points of libeva_moe.so (declared in include/eva_moe.h).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+
+#include "internal.h"
+
+namespace eva {
+
+static size_t up256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
+
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows)
+{
+    WsLayout L{};
+    L.max_rows = max_rows;
+    L.S = max_rows * s.topk;
+    L.R = L.S + (max_rows + RUN_ROWS - 1) / RUN_ROWS;
+    L.imax = std::max(s.inter, s.shared_inter);
+    L.nchA = L.imax / 128;
+    L.nchH = s.hidden / 128;
+    L.ks_router = (s.hidden + ROUTER_KSLICE - 1) / ROUTER_KSLICE;
+    const size_t S = L.S, R = L.R, M = max_rows, H = s.hidden, E = s.n_experts;
+    const size_t St = S + M;
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o += up256(bytes);
+        return at;
+    };
+    L.status = take(256);
+    const CtrLayout C = ctr_layout(L);
+    L.n_counters = C.n;
+    L.counters = take(C.n * 4);
+    L.runs = take((2 + 2 * S + 1) * 4);
+    L.run_expert = take(S * 4);
+    L.estart = take((E + 1) * 4);
+    L.slot_act = take(S * 4);
+    L.tok_expect = take(M * 4);
+    const size_t lrows = std::max(static_cast<size_t>(L.ks_router) * std::min<size_t>(M, 32), M);
+    L.logits = take(lrows * E * 4);
+    L.idx = take(M * s.topk * 4);
+    L.w = take(M * s.topk * 4);
+    L.xrot = take(2 * St * H * 2);
+    L.act = take(St * L.imax * 2);
+    L.dpart = take(St * H * 4);
+    const size_t pa = std::min<size_t>(PARTA_ITEMS, R * L.nchA * 4);
+    L.partA = take(pa * 2 * RUN_ROWS * 128 * 4);
+    L.total = o;
+    return L;
+}
+
+CtrLayout ctr_layout(const WsLayout& L)
+{
+    CtrLayout C{};
+    C.work = 0;
+    C.ctr0 = 32;
+    C.ctrA = C.ctr0 + L.R;
+    C.ctrAk = C.ctrA + L.R;
+    C.ctrB = C.ctrAk + L.R * L.nchA;
+    C.n = C.ctrB + L.max_rows * L.nchH;
+    return C;
+}
+
+int num_sms()
+{
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (!cached[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 1;
+    }
+    return cached[dev];
+}
+
+static bool shape_ok(const EvaMoeShape* s)
+{
+    if (!s) return false;
+    if (s->hidden <= 0 || s->hidden % 256) return false;
+    if (s->inter <= 0 || s->inter % 128) return false;
+    if (s->n_experts < 1 || s->n_experts > 1024) return false;
+    if (s->topk < 1 || s->topk > 32 || s->topk > s->n_experts) return false;
+    if (s->bits < 2 || s->bits > 4) return false;
+    if (s->shared_inter < 0 || s->shared_inter % 128) return false;
+    if (s->shared_inter && (s->shared_bits < 2 || s->shared_bits > 4)) return false;
+    if (s->router < 0 || s->router > 2) return false;
+    if (s->n_group < 1 || s->n_group > 32 || s->n_experts % s->n_group) return false;
+    if (s->topk_group < 1 || s->topk_group > s->n_group) return false;
+    if (s->n_group > 1 && s->topk > s->topk_group * (s->n_experts / s->n_group)) return false;
+    if (s->act_routed < 0 || s->act_routed > 1 || s->act_shared < 0 || s->act_shared > 1) return false;
+    return true;
+}
+
+static bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+static int cuda_status(cudaError_t e) { return e == cudaSuccess ? EVA_OK : EVA_ERR_CUDA; }
+
+static void fill_permute(PermuteArgs& pa, const EvaMoeShape& s, const void* sel, int sel64, const float* rw, int M,
+                         int capacity)
+{
+    std::memset(&pa, 0, sizeof(pa));
+    pa.sel = sel;
+    pa.sel64 = sel64;
+    pa.rw = rw;
+    pa.M = M;
+    pa.topk = s.topk;
+    pa.n_local = s.n_experts;
+    pa.capacity = capacity;
+    pa.has_shared = s.shared_inter > 0;
+    pa.H = s.hidden;
+}
+
+}  // namespace eva
+
+using namespace eva;
+
+extern "C" {
+
+size_t eva_moe_workspace_bytes(const EvaMoeShape* shape, int32_t max_rows)
+{
+    if (!shape_ok(shape) || max_rows < 1) return 0;
+    return ws_layout(*shape, max_rows).total;
+}
+
+int eva_moe_clear_status(void* workspace, void* stream)
+{
+    if (!workspace) return EVA_ERR_INVALID;
+    return cuda_status(cudaMemsetAsync(workspace, 0, 4, static_cast<cudaStream_t>(stream)));
+}
+
+int eva_moe_read_status(const void* workspace, int32_t* status_host, void* stream)
+{
+    if (!workspace || !status_host) return EVA_ERR_INVALID;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(status_host, workspace, 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return cuda_status(e);
+}
+
+int eva_moe_topk(const EvaMoeShape* shape, const float* logits, int32_t M, const float* router_b,
+                 int32_t* idx_out, float* w_out, void* stream)
+{
+    if (!shape_ok(shape) || M < 0 || !logits || !idx_out || !w_out) return EVA_ERR_INVALID;
+    if (M == 0) return EVA_OK;
+    return cuda_status(launch_topk(*shape, logits, 1, M, router_b, nullptr, idx_out, w_out, static_cast<cudaStream_t>(stream)));
+}
+
+int eva_moe_route(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const float* router_w,
+                  const float* router_b, float* logits_out, int32_t* idx_out, float* w_out, void* workspace,
+                  size_t workspace_bytes, void* stream)
+{
+    if (!shape_ok(shape) || M < 0 || !x || !router_w || !idx_out || !w_out || !workspace) return EVA_ERR_INVALID;
+    if (!aligned(x, 8) || !aligned(router_w, 16)) return EVA_ERR_INVALID;
+    if (M == 0) return EVA_OK;
+    const WsLayout L = ws_layout(*shape, M);
+    if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + L.logits);
+    int ks = 1;
+    cudaError_t e = launch_router_logits(x, x_is_bf16 ? 1 : 0, M, shape->hidden, shape->n_experts, router_w, part, &ks, st);
+    if (e != cudaSuccess) return EVA_ERR_CUDA;
+    return cuda_status(launch_topk(*shape, part, ks, M, router_b, logits_out, idx_out, w_out, st));
+}
+
+int eva_moe_permute(const EvaMoeShape* shape, const void* sel, int32_t sel_is_i64, const float* rw, int32_t M,
+                    int32_t capacity, int32_t* runs, int32_t* expert_start, void* stream)
+{
+    if (!shape_ok(shape) || M < 0 || !sel || !rw || !runs || capacity < M || capacity < 1) return EVA_ERR_INVALID;
+    if (static_cast<long long>(capacity) * shape->topk > 65535 * 16) return EVA_ERR_INVALID;
+    PermuteArgs pa;
+    fill_permute(pa, *shape, sel, sel_is_i64 ? 1 : 0, rw, M, capacity);
+    pa.runs = runs;
+    pa.estart = expert_start;
+    return cuda_status(launch_permute(pa, static_cast<cudaStream_t>(stream)));
+}
+
+static int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
+                        int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
+                        void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st)
+{
+    if (!shape_ok(shape) || M < 0 || !x || !sel || !rw || !tables || !workspace) return EVA_ERR_INVALID;
+    if (!out_f32 && !out_bf16) return EVA_ERR_INVALID;
+    if (shape->shared_inter && !shared) return EVA_ERR_INVALID;
+    if (!aligned(x, 8) || !aligned(out_f32, 16) || !aligned(out_bf16, 8)) return EVA_ERR_INVALID;
+    for (int i = 0; i < 9; ++i)
+        if (!tables[i]) return EVA_ERR_INVALID;
+    if (M == 0) return EVA_OK;
+    const WsLayout L = ws_layout(*shape, M);
+    if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    PermuteArgs pa;
+    fill_permute(pa, *shape, sel, sel_is_i64 ? 1 : 0, rw, M, M);
+    for (int i = 0; i < 9; ++i) pa.tables[i] = tables[i];
+    pa.runs = reinterpret_cast<int32_t*>(ws + L.runs);
+    pa.run_expert = reinterpret_cast<int32_t*>(ws + L.run_expert);
+    pa.estart = reinterpret_cast<int32_t*>(ws + L.estart);
+    pa.slot_act = reinterpret_cast<int32_t*>(ws + L.slot_act);
+    pa.tok_expect = reinterpret_cast<int32_t*>(ws + L.tok_expect);
+    pa.counters = reinterpret_cast<int32_t*>(ws + L.counters);
+    pa.n_counters = static_cast<int>(L.n_counters);
+    pa.status = reinterpret_cast<int32_t*>(ws + L.status);
+    pa.out_f32 = out_f32;
+    pa.out_bf16 = out_bf16;
+    cudaError_t e = launch_permute(pa, st);
+    if (e != cudaSuccess) return EVA_ERR_CUDA;
+    ExpertsArgs ea;
+    std::memset(&ea, 0, sizeof(ea));
+    ea.shape = shape;
+    ea.x = x;
+    ea.x_bf16 = x_is_bf16 ? 1 : 0;
+    ea.M = M;
+    ea.sel = sel;
+    ea.sel64 = sel_is_i64 ? 1 : 0;
+    ea.rw = rw;
+    for (int i = 0; i < 9; ++i) {
+        ea.tables[i] = tables[i];
+        ea.shared[i] = shape->shared_inter ? shared[i] : 0;
+    }
+    ea.ws = workspace;
+    ea.L = L;
+    ea.out_f32 = out_f32;
+    ea.out_bf16 = out_bf16;
+    return cuda_status(launch_experts(ea, st));
+}
+
+int eva_moe_experts(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
+                    int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
+                    void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream)
+{
+    return experts_impl(shape, x, x_is_bf16, M, sel, sel_is_i64, rw, tables, shared, workspace, workspace_bytes,
+                        out_f32, out_bf16, static_cast<cudaStream_t>(stream));
+}
+
+int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const float* router_w,
+                    const float* router_b, const int64_t* const* tables, const int64_t* shared, void* workspace,
+                    size_t workspace_bytes, float* out_f32, void* out_bf16, float* logits_out, int32_t* idx_out,
+                    float* w_out, void* stream)
+{
+    if (!shape_ok(shape) || M < 0 || !workspace) return EVA_ERR_INVALID;
+    if (M == 0) return EVA_OK;
+    const WsLayout L = ws_layout(*shape, M);
+    if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int32_t* idx = idx_out ? idx_out : reinterpret_cast<int32_t*>(ws + L.idx);
+    float* w = w_out ? w_out : reinterpret_cast<float*>(ws + L.w);
+    int rc = eva_moe_route(shape, x, x_is_bf16, M, router_w, router_b, logits_out, idx, w, workspace, workspace_bytes, stream);
+    if (rc != EVA_OK) return rc;
+    return experts_impl(shape, x, x_is_bf16, M, idx, 0, w, tables, shared, workspace, workspace_bytes, out_f32, out_bf16,
+                        static_cast<cudaStream_t>(stream));
+}
+
+int eva_exl3_dequant(const void* trellis, int32_t in_features, int32_t out_features, int32_t bits, uint16_t* w_out,
+                     void* stream)
+{
+    if (!trellis || !w_out || in_features <= 0 || out_features <= 0 || in_features % 16 || out_features % 16) return EVA_ERR_INVALID;
+    if (bits < 2 || bits > 4 || !aligned(trellis, 4)) return EVA_ERR_INVALID;
+    return cuda_status(launch_dequant(trellis, in_features, out_features, bits, w_out, static_cast<cudaStream_t>(stream)));
+}
+
+int32_t eva_moe_arch(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,75 @@
+// Host-side declarations shared by the eva_b200 CUDA translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/eva_moe.h"
+
+namespace eva {
+
+constexpr int RUN_ROWS = 8;          // slots of one expert per run (MMA N dimension)
+constexpr int PARTA_ITEMS = 4096;    // split-k partial buffers of the gate/up stage
+constexpr int ROUTER_KSLICE = 512;   // k elements per router GEMV warp
+
+// Byte offsets of the workspace regions for calls of up to max_rows tokens.
+struct WsLayout {
+    int max_rows, S, R, imax, nchA, nchH, ks_router;
+    size_t status, counters, n_counters, runs, run_expert, estart, slot_act, tok_expect;
+    size_t logits, idx, w, xrot, act, dpart, partA, total;
+};
+
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows);
+
+// Counter block layout inside `counters` (int32 indices).
+struct CtrLayout {
+    int work, ctr0, ctrA, ctrAk, ctrB, n;
+};
+CtrLayout ctr_layout(const WsLayout& L);
+
+cudaError_t launch_router_logits(const void* x, int x_bf16, int M, int H, int E, const float* W, float* part,
+                                 int* ks_used, cudaStream_t stream);
+cudaError_t launch_topk(const EvaMoeShape& s, const float* part, int ks, int M, const float* bias,
+                        float* logits_out, int32_t* idx, float* w, cudaStream_t stream);
+
+struct PermuteArgs {
+    const void* sel;
+    int sel64;
+    const float* rw;
+    int M, topk, n_local, capacity, has_shared, H;
+    const int64_t* tables[9];   // may be null: no pointer validation
+    int32_t* runs;
+    int32_t* run_expert;        // may be null
+    int32_t* estart;            // may be null
+    int32_t* slot_act;          // may be null
+    int32_t* tok_expect;        // may be null
+    int32_t* counters;          // zeroed when non-null
+    int n_counters;
+    int32_t* status;            // may be null
+    float* out_f32;             // rows with no arrivals are zeroed (may be null)
+    void* out_bf16;
+};
+cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t stream);
+
+struct ExpertsArgs {
+    const EvaMoeShape* shape;
+    const void* x;
+    int x_bf16, M;
+    const void* sel;
+    int sel64;
+    const float* rw;
+    const int64_t* tables[9];
+    int64_t shared[9];
+    void* ws;
+    WsLayout L;
+    float* out_f32;
+    void* out_bf16;
+};
+cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream);
+
+cudaError_t launch_dequant(const void* trellis, int in, int out, int K, uint16_t* w, cudaStream_t stream);
+
+int num_sms();
+
+}  // namespace eva

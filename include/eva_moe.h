@@ -1,0 +1,134 @@
+/*
+ * eva_moe.h - C ABI of the B200 (sm_100a) DeepSeek MoE hot path.
+ *
+ * Plain pointers and sizes only. Device pointers are CUDA device addresses; `stream` is a
+ * cudaStream_t passed as void*. Every entry point is asynchronous on `stream`, performs no
+ * host<->device synchronisation and no allocation, and returns an EVA_* status for argument and
+ * launch errors. Device-side problems (expert id outside the tables, an unbound pointer, a bounded
+ * wait that gave up) are OR-ed into a status word inside the workspace; read it with
+ * eva_moe_read_status() after the stream has reached that point.
+ *
+ * Reference interfaces replaced (paths within the Findddx/eva project):
+ *   eva_moe_experts     runtime/ds41/csrc/moe_coop2048/binding.cu:73-145 `run(x, sel, rw, tables[9],
+ *                       scratch[8], k, limit, check_bounds)` (also moe_coop512/binding.cu:71-146 and
+ *                       moe_coop3072/moe_coop3072.cu:42-176): routed EXL3 experts + combine
+ *                       (+ the shared expert, which the reference runs separately through
+ *                       exllamav3 LinearEXL3, runtime/ds41/model.py:441-452).
+ *   eva_moe_permute     runtime/ds41/csrc/moe_coop2048/binding.cu:149-174 `prepare_routes(sel, rw, runs,
+ *                       capacity, n_local)`: the int32 run table [n_runs, 0, run_start[S+1], order[S]].
+ *   eva_moe_route       runtime/ds41/model.py:404-416 `Block.route(x)` (FP32 logits, scoring, biased top-k,
+ *                       normalised weights).
+ *   eva_moe_topk        the scoring/top-k half of Block.route, from given FP32 logits.
+ *   eva_moe_forward     runtime/ds41/model.py:454-499 `Block.experts(x)` (route + experts + shared).
+ *   eva_exl3_dequant    the vendored ExLlamaV3 dq_dispatch<K, mul1> decode
+ *                       (runtime/ds41/csrc/moe_coop2048/vendor/quant/exl3_dq.cuh:287-330), as a
+ *                       standalone projection dequantiser.
+ */
+#ifndef EVA_MOE_H
+#define EVA_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* return codes */
+#define EVA_OK 0
+#define EVA_ERR_INVALID 1      /* bad argument: shape, null pointer, unsupported K, alignment */
+#define EVA_ERR_CUDA 2         /* a CUDA launch or runtime call failed */
+#define EVA_ERR_WORKSPACE 3    /* workspace smaller than eva_moe_workspace_bytes() */
+
+/* device status bits (eva_moe_read_status) */
+#define EVA_STATUS_BAD_EXPERT 1   /* a selected expert id is outside [0, n_local) or has a zero pointer */
+#define EVA_STATUS_TIMEOUT 2      /* a bounded device wait gave up (results of that call are invalid) */
+#define EVA_STATUS_CAPACITY 4     /* more rows than the workspace was sized for */
+
+/* router kinds */
+#define EVA_ROUTER_SOFTMAX 0       /* DeepSeek-V2-Lite greedy top-k over softmax probabilities */
+#define EVA_ROUTER_SIGMOID 1       /* DeepSeek-V3: sigmoid + bias, group-limited top-k */
+#define EVA_ROUTER_SQRTSOFTPLUS 2  /* eva DS4.1: sqrt(softplus) + bias top-k (model.py:404-416) */
+
+/* activation modes of the gated MLP */
+#define EVA_ACT_CLAMP_AFTER 0     /* silu(g) then clamp (MoE coop act_gate, exl3_moe_coop_kernel.cuh:115-129) */
+#define EVA_ACT_CLAMP_BEFORE 1    /* clamp then silu(g) * u (torch swiglu, kernels.py:213-217) */
+
+typedef struct EvaMoeShape {
+    int32_t hidden;        /* H, multiple of 256 */
+    int32_t inter;         /* routed expert intermediate width I, multiple of 128 */
+    int32_t n_experts;     /* routed experts in the pointer tables (n_local) */
+    int32_t topk;          /* selected experts per token, 1..32 */
+    int32_t bits;          /* EXL3 K of the routed experts: 2, 3 or 4 */
+    int32_t shared_inter;  /* shared expert intermediate width, 0 = no shared expert */
+    int32_t shared_bits;   /* EXL3 K of the shared expert */
+    int32_t router;        /* EVA_ROUTER_* */
+    int32_t n_group;       /* group-limited routing: number of groups (1 = off) */
+    int32_t topk_group;    /* groups kept per token */
+    int32_t norm_topk;     /* renormalise the selected weights (sum + 1e-20) */
+    int32_t act_routed;    /* EVA_ACT_* for routed experts */
+    int32_t act_shared;    /* EVA_ACT_* for the shared expert */
+    float route_scale;     /* routed_scaling_factor / route_scale */
+    float swiglu_limit;    /* 0 = no clamp */
+} EvaMoeShape;
+
+/* Bytes of device workspace needed for calls of up to `max_rows` tokens. */
+size_t eva_moe_workspace_bytes(const EvaMoeShape* shape, int32_t max_rows);
+
+/* Clears the workspace's status word (asynchronous). */
+int eva_moe_clear_status(void* workspace, void* stream);
+
+/* Copies the status word to *status_host (synchronises `stream`). */
+int eva_moe_read_status(const void* workspace, int32_t* status_host, void* stream);
+
+/* Router: logits_out (may be NULL) float [M][E]; idx_out int32 [M][topk]; w_out float [M][topk].
+ * x is bf16 (x_is_bf16 = 1) or fp16 [M][H]; router_w float [E][H]; router_b float [E] (NULL = 0). */
+int eva_moe_route(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
+                  const float* router_w, const float* router_b, float* logits_out,
+                  int32_t* idx_out, float* w_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Scoring + top-k from FP32 logits [M][E] (router_b may be NULL). */
+int eva_moe_topk(const EvaMoeShape* shape, const float* logits, int32_t M, const float* router_b,
+                 int32_t* idx_out, float* w_out, void* stream);
+
+/* Permutation. sel: [M][topk] int32 (sel_is_i64 = 0) or int64; rw: float [M][topk] (0 = inactive).
+ * runs: int32 [2 + 2 * capacity * topk + 1] in the reference layout
+ *       [n_runs, 0, run_start[S + 1], order[S]], S = capacity * topk, unused entries zero.
+ * expert_start (may be NULL): int32 [n_local + 1], exclusive prefix of active slots per expert. */
+int eva_moe_permute(const EvaMoeShape* shape, const void* sel, int32_t sel_is_i64, const float* rw,
+                    int32_t M, int32_t capacity, int32_t* runs, int32_t* expert_start, void* stream);
+
+/* Fused experts: permutation + rotation + gate/up + activation + down + routed combine + shared
+ * expert, one persistent launch after the permutation.
+ *   x:        [M][H] bf16 or fp16 (x_is_bf16)
+ *   sel, rw:  as eva_moe_permute
+ *   tables:   host array of 9 device pointers, each an int64 [n_experts] table of device addresses in
+ *             the reference row order [g.trellis, g.suh, g.svh, u.trellis, u.suh, u.svh, d.trellis,
+ *             d.suh, d.svh] (runtime/ds41/cache.py:1864-1887); 0 = unbound
+ *   shared:   host array of 9 device addresses of the shared expert (NULL when shape->shared_inter == 0)
+ *   out_f32:  float [M][H] or NULL; out_bf16: bf16 [M][H] or NULL (at least one)
+ */
+int eva_moe_experts(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
+                    const void* sel, int32_t sel_is_i64, const float* rw,
+                    const int64_t* const* tables, const int64_t* shared,
+                    void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream);
+
+/* Whole layer: eva_moe_route + eva_moe_experts. idx_out / w_out / logits_out may be NULL. */
+int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
+                    const float* router_w, const float* router_b,
+                    const int64_t* const* tables, const int64_t* shared,
+                    void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16,
+                    float* logits_out, int32_t* idx_out, float* w_out, void* stream);
+
+/* Dequantise one EXL3 projection: trellis int16 [in/16][out/16][16K] -> fp16 bits [in][out]. */
+int eva_exl3_dequant(const void* trellis, int32_t in_features, int32_t out_features, int32_t bits,
+                     uint16_t* w_out, void* stream);
+
+/* Library identification: sm arch the kernels were built for (100 for sm_100a). */
+int32_t eva_moe_arch(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EVA_MOE_H */

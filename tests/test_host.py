@@ -1,0 +1,117 @@
+"""Host logic without a GPU: configs, expert records and handles, routers, permutation oracle,
+the C ABI library's exports. CPU only."""
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from eva_b200 import config as C
+from eva_b200 import experts as X
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_config_validation():
+    with pytest.raises(ValueError):
+        C.MoEConfig("bad", hidden=100, inter=128, n_experts=8, topk=2, router="softmax")
+    with pytest.raises(ValueError):
+        C.MoEConfig("bad", hidden=256, inter=128, n_experts=8, topk=2, router="nope")
+    with pytest.raises(ValueError):
+        C.MoEConfig("bad", hidden=256, inter=128, n_experts=8, topk=2, router="sigmoid", n_group=3)
+    assert C.V3.expert_bytes() == 16_515_072 + 6 * (7168 + 2048)
+
+
+def test_record_layout_matches_pack_format():
+    offs, rec, shapes = X.record_layout(256, 128, 3)
+    # w1 (gate), w2 (down), w3 (up); each suh, svh, trellis (tools/pack_exl3.py:93-107)
+    order = sorted(offs.items(), key=lambda kv: kv[1][0])
+    assert [k for k, _ in order] == [("gate", "suh"), ("gate", "svh"), ("gate", "trellis"),
+                                     ("down", "suh"), ("down", "svh"), ("down", "trellis"),
+                                     ("up", "suh"), ("up", "svh"), ("up", "trellis")]
+    assert rec % 4096 == 0
+    assert all(o % 16 == 0 for o, _ in offs.values())
+
+
+def test_pointer_tables_address_the_tensors():
+    cfg = C.MoEConfig("t", hidden=256, inter=128, n_experts=4, topk=2, router="softmax", shared_inter=256, bits=2)
+    layer = X.make_layer(cfg, "cpu", seed=1)
+    for e in range(4):
+        for (proj, kind), row in X.ROW.items():
+            assert int(layer.packed[row, e]) == layer.tensor(e, proj, kind).data_ptr()
+    for (proj, kind), row in X.ROW.items():
+        assert int(layer.shared[row]) == layer.tensor(-1, proj, kind).data_ptr()
+    t = layer.tensor(2, "down", "trellis")
+    assert tuple(t.shape) == (128 // 16, 256 // 16, 32)
+    suh = layer.tensor(0, "gate", "suh").float()
+    assert torch.all(suh.abs() >= 0.74) and torch.all(suh.abs() <= 1.26)
+
+
+def test_sigmoid_group_limited_route_properties(oracle):
+    cfg = C.V3
+    rng = np.random.default_rng(0)
+    logits = rng.standard_normal((64, cfg.n_experts)).astype(np.float32) * 1.7
+    bias = (rng.standard_normal(cfg.n_experts) * 0.01).astype(np.float32)
+    idx, w = oracle.route(logits, bias, cfg)
+    groups = idx // (cfg.n_experts // cfg.n_group)
+    assert all(len(set(g)) <= cfg.topk_group for g in groups)
+    assert np.allclose(w.sum(-1), cfg.route_scale, rtol=1e-5)
+    assert all(len(set(r)) == cfg.topk for r in idx)
+    # without grouping it is plain biased top-k
+    flat = cfg.with_(n_group=1, topk_group=1)
+    idx2, _ = oracle.route(logits, bias, flat)
+    s = oracle.scores(logits, "sigmoid") + bias
+    assert np.array_equal(np.sort(idx2, -1), np.sort(np.argsort(-s, -1, kind="stable")[:, :cfg.topk], -1))
+
+
+def test_softmax_route_unnormalised(oracle):
+    cfg = C.V2_LITE
+    rng = np.random.default_rng(1)
+    logits = rng.standard_normal((16, cfg.n_experts)).astype(np.float32)
+    idx, w = oracle.route(logits, np.zeros(cfg.n_experts, np.float32), cfg)
+    p = np.exp(logits - logits.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    assert np.allclose(w, np.take_along_axis(p, idx, -1), rtol=1e-6)
+    assert np.array_equal(idx, np.argsort(-logits, -1, kind="stable")[:, :cfg.topk])
+
+
+def test_run_table_edge_cases(oracle):
+    # all inactive
+    t = oracle.run_table(np.array([[3, 4]]), np.array([[0.0, 0.0]], np.float32), 2)
+    assert t[0] == 0 and all(v == 0 for v in t)
+    # one expert picked by 20 slots -> runs of 8, 8, 4
+    sel = np.array([[5, i] for i in range(20)])[:, :1].repeat(2, 1)
+    sel[:, 1] = np.arange(20) + 6
+    t = oracle.run_table(sel, None, 20)
+    S = 40
+    starts = t[2:2 + t[0] + 1]
+    assert t[0] == 3 + 20 and starts[:4] == [0, 8, 16, 20]
+    order = t[2 + S + 1: 2 + S + 1 + 40]
+    assert order[:20] == [2 * i for i in range(20)]
+
+
+def test_c_abi_exports_every_declared_symbol():
+    from eva_b200 import _lib
+    L = _lib.load()
+    header = (ROOT / "include" / "eva_moe.h").read_text()
+    declared = set(re.findall(r"\b(eva_[a-z0-9_]+)\s*\(", header))
+    assert declared == set(_lib.EXPORTS)
+    for name in declared:
+        assert hasattr(L, name)
+    assert L.eva_moe_arch() == 100
+    for cfg in (C.V3, C.V2_LITE, C.REF_NATIVE):
+        sh = _lib.shape_of(cfg)
+        assert L.eva_moe_workspace_bytes(ctypes.byref(sh), 64) > 0
+    bad = _lib.shape_of(C.V3)
+    bad.bits = 5
+    assert L.eva_moe_workspace_bytes(ctypes.byref(bad), 64) == 0
+    # argument errors are reported without touching a GPU
+    assert L.eva_exl3_dequant(None, 16, 16, 3, None, None) == _lib.EVA_ERR_INVALID
+
+
+def test_library_has_no_torch_dependency():
+    import subprocess
+    out = subprocess.run(["ldd", str(ROOT / "eva_b200" / "libeva_moe.so")], capture_output=True, text=True).stdout
+    assert "torch" not in out and "c10" not in out
