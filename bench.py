@@ -1,0 +1,355 @@
+"""Benchmark of the B200 DeepSeek MoE hot path (one JSON line on rank 0).
+
+Workload (N = 1): one DeepSeek-V3-shape MoE layer in decode (hidden 7168, 256 routed experts top-8
+sigmoid group-limited n_group 8 / topk_group 4 with e_score_correction_bias, routed_scaling 2.5,
+expert intermediate 2048, 1 shared expert, EXL3 K = 3 = 4.24 GB of experts), batch of --batch
+tokens (default 8) per step. A step = router -> permutation -> fused experts -> combine + shared.
+Each step routes a different pre-generated batch, so the experts touched change from step to step
+and the 4.24 GB of expert weights never fit the 126 MB L2 (inputs larger than L2; no flush).
+
+value     tokens/s with inputs already in HBM, timed with CUDA events on the launching stream.
+e2e       tokens/s through the public API (EvaMoE.forward) with the batch copied from pinned host
+          memory and the result copied back inside the timed region.
+roofline  the fused experts launch (eva_moe_experts: permutation + experts kernel): algorithmic
+          bytes = U * R + S (U distinct routed experts of the step, R bytes per expert record, S the
+          shared expert record) over its event-timed duration, against MEASURED_PEAKS.json hbm_gbs.
+cpu_baseline  the CPU oracle port (C restatement + numpy router) on the host cores, rank 0, N = 1,
+          on a bounded sample of the same workload.
+
+N > 1 (torchrun): every rank runs its own replica of the layer with its own token batches
+(replicas, weak scaling); value = all ranks' tokens / max over ranks of the timed region.
+
+--impl reference: the reference's CPU path restated (oracle port) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "moe_layer_decode_tokens_per_s"
+UNIT = "tokens/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="eva", choices=["eva", "reference"])
+    ap.add_argument("--config", default="v3")
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--small", action="store_true", help="small case for ncu captures (64 experts)")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 50 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_sample(cfg, layer_host, x_bits, threads):
+    """Oracle port on one token: FP64 router + routed experts + shared (seconds, tokens)."""
+    import numpy as np
+    from oracle import oracle as O
+    x1 = x_bits[:1]
+    t0 = time.perf_counter()
+    logits = O.router_logits(O.bf16_to_f32(x1), layer_host.router_w.numpy())
+    idx, w = O.route(logits, layer_host.router_b.numpy(), cfg)
+    O.moe_forward(x1, idx, w, layer_host, threads=threads)
+    return time.perf_counter() - t0, 1
+
+
+def run_reference(args):
+    """--impl reference: the CPU restatement of the path, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+    from eva_b200.config import CONFIGS
+    from eva_b200.experts import make_layer
+    from oracle import oracle as O
+    cfg = CONFIGS[args.config]
+    threads = os.cpu_count() or 1
+    # the sample only touches the experts its token selects: build them on the host lazily by
+    # generating the whole layer on the host would take minutes at 4 GB, so the layer is built with
+    # every expert sharing 8 distinct records (same bytes per expert, same arithmetic)
+    layer = make_layer(cfg, "cpu", seed=0, n_fill=8)
+    from eva_b200.experts import replicate_experts
+    replicate_experts(layer, 8)
+    g = torch.Generator().manual_seed(1)
+    xs = torch.randn(args.steps + args.warmup, cfg.hidden, generator=g).to(torch.bfloat16)
+    xb = xs.view(torch.int16).numpy().view(np.uint16)
+    for i in range(args.warmup):
+        cpu_sample(cfg, layer, xb[i:i + 1], threads)
+    times = []
+    for i in range(args.steps):
+        dt, n = cpu_sample(cfg, layer, xb[args.warmup + i: args.warmup + i + 1], threads)
+        times.append(dt)
+    total = sum(times)
+    value = args.steps / total
+    sample = f"1 token per step (FP64 router + its {cfg.topk} routed experts + shared expert, EXL3 dequantised)"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} MoE layer decode, CPU restatement", "batch": 1},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from eva_b200 import _lib
+    from eva_b200.config import CONFIGS
+    from eva_b200.experts import make_layer
+    from eva_b200.runner import EvaMoE
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    cfg = CONFIGS[args.config]
+    if args.small:
+        cfg = cfg.with_(n_experts=64, n_group=8, topk_group=4)
+    M = args.batch
+    steps, warmup = args.steps, max(3, args.warmup)
+    layer = make_layer(cfg, dev, seed=0)
+    moe = EvaMoE(layer, max_rows=max(M, 8))
+    stream = torch.cuda.current_stream(dev)
+    nb = steps + warmup
+    g = torch.Generator(device=dev)
+    g.manual_seed(1 + rank)
+    xs = torch.randn(nb, M, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    idx_all = torch.empty(nb, M, cfg.topk, dtype=torch.int32, device=dev)
+    w_all = torch.empty(nb, M, cfg.topk, device=dev)
+    # routes of every batch (for the algorithmic byte count; the timed steps route again)
+    for i in range(nb):
+        moe.forward(xs[i], out=out, idx_out=idx_all[i], w_out=w_all[i])
+    torch.cuda.synchronize()
+    if moe.status():
+        raise RuntimeError(f"device status {moe.status():#x}")
+    idx_host = idx_all.cpu().numpy()
+
+    lib = _lib.load()
+    import ctypes
+    shape = moe.shape
+    tables, shared = moe._tables, moe._shared
+    ws = moe.workspace
+    routed_rec = 3 * cfg.hidden * cfg.inter * cfg.bits // 8 + 6 * (cfg.hidden + cfg.inter)
+    shared_rec = (3 * cfg.hidden * cfg.shared_inter * cfg.shared_bits // 8 + 6 * (cfg.hidden + cfg.shared_inter)
+                  if cfg.shared_inter else 0)
+    router_bytes = cfg.n_experts * cfg.hidden * 4 + cfg.n_experts * 4
+
+    def step(i, ev=None):
+        x = xs[i]
+        rc = lib.eva_moe_route(ctypes.byref(shape), x.data_ptr(), 1, M, layer.router_w.data_ptr(),
+                               layer.router_b.data_ptr(), None, idx_all[i].data_ptr(), w_all[i].data_ptr(),
+                               ws.data_ptr(), ws.numel(), stream.cuda_stream)
+        _lib.check(rc, "route")
+        if ev is not None:
+            ev[0].record(stream)
+        rc = lib.eva_moe_experts(ctypes.byref(shape), x.data_ptr(), 1, M, idx_all[i].data_ptr(), 0,
+                                 w_all[i].data_ptr(), tables, shared, ws.data_ptr(), ws.numel(), None,
+                                 out.data_ptr(), stream.cuda_stream)
+        _lib.check(rc, "experts")
+        if ev is not None:
+            ev[1].record(stream)
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0.record(stream)
+        for i in range(steps):
+            step(warmup + i, evs[i])
+        t1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms_total = t0.elapsed_time(t1)
+    exp_ms = [a.elapsed_time(b) for a, b in evs]
+    if world > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    st = moe.status()
+
+    # ---- end to end through the public API with host buffers --------------------------------
+    xh = xs.cpu().pin_memory()
+    oh = torch.empty(M, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+    xdev = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    for i in range(warmup):
+        xdev.copy_(xh[i], non_blocking=True)
+        y = moe.forward(xdev, out=out)
+        oh.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        xdev.copy_(xh[warmup + i], non_blocking=True)
+        y = moe.forward(xdev, out=out)
+        oh.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # ---- roofline of the fused experts launch -------------------------------------------------
+    U = [len(np.unique(idx_host[warmup + i])) for i in range(steps)]
+    alg_bytes = [u * routed_rec + shared_rec for u in U]
+    achieved = statistics.mean(b / (ms * 1e-3) for b, ms in zip(alg_bytes, exp_ms)) / 1e9
+    peak, peak_kind = peaks()
+    traffic = None
+    prof = ROOT / "profiles" / "experts_kernel_traffic.txt"
+    if prof.exists():
+        try:
+            per_expert = float(prof.read_text().split("bytes_per_expert_record_equivalent:")[1].split()[0])
+            traffic = per_expert * (statistics.mean(U) + (shared_rec / routed_rec if routed_rec else 0))
+        except (IndexError, ValueError):
+            traffic = None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from eva_b200.experts import replicate_experts
+        host = make_layer(cfg, "cpu", seed=0, n_fill=8)
+        replicate_experts(host, 8)
+        xb = xs[0].cpu().view(torch.int16).numpy().view(np.uint16)
+        threads = os.cpu_count() or 1
+        cpu_sample(cfg, host, xb, threads)   # warm-up
+        ts = []
+        t_end = time.perf_counter() + 20.0
+        while time.perf_counter() < t_end and len(ts) < 5:
+            dt, _ = cpu_sample(cfg, host, xb[len(ts) % M:], threads)
+            ts.append(dt)
+        cpu = {"value": len(ts) / sum(ts), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{len(ts)} single-token steps (FP64 router + top-{cfg.topk} routed experts + shared, "
+                         f"EXL3 dequantised by the C restatement)"}
+
+    tokens = M * steps * world
+    line = {
+        "metric": METRIC, "value": tokens / (ms_total * 1e-3), "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": ms_total / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp16 (EXL3 K3 weights decoded to fp16, fp32 accumulate), bf16 in/out",
+        "data": "synthetic (seeded random EXL3 trellis codes, N(0,1) bf16 hidden states)",
+        "config": {"workload": f"DeepSeek-{cfg.name.upper()} MoE layer decode (EXL3 K{cfg.bits}), batch {M} tokens/step"
+                               + (" [small]" if args.small else ""),
+                   "hidden": cfg.hidden, "experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
+                   "shared_inter": cfg.shared_inter, "bits": cfg.bits, "batch": M,
+                   "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (4.24 GB experts, different routes every step)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_kind": peak_kind, "kernel": "eva_moe_experts (permute + experts_kernel)",
+                     "alg_bytes_per_launch": statistics.mean(alg_bytes), "launch_ms": statistics.mean(exp_ms),
+                     "distinct_experts_per_step": statistics.mean(U)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": M * cfg.hidden * 2,
+                "d2h_bytes_per_step": M * cfg.hidden * 2},
+        "gpu_launches": 4 * steps,
+        "clocks": clocks.summary(),
+        "device_status": st,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -186,7 +186,10 @@ static int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf
     if (shape->shared_inter && !shared) return EVA_ERR_INVALID;
     if (!aligned(x, 8) || !aligned(out_f32, 16) || !aligned(out_bf16, 8)) return EVA_ERR_INVALID;
     for (int i = 0; i < 9; ++i)
-        if (!tables[i]) return EVA_ERR_INVALID;
+        if (!tables[i] || !aligned(tables[i], 8)) return EVA_ERR_INVALID;
+    if (shape->shared_inter)
+        for (int i = 0; i < 9; ++i)
+            if (shared[i] == 0 || (shared[i] & 15)) return EVA_ERR_INVALID;   // bulk copies need 16 B
     if (M == 0) return EVA_OK;
     const WsLayout L = ws_layout(*shape, M);
     if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;

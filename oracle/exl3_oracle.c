@@ -296,7 +296,7 @@ void eo_expert(const double* x, int M, int H, int I, int Ho,
 /* ---------------------------------------------------------------------------------------------
  * Routed MoE forward from EXL3 tensors (dequantized on the fly, one expert at a time).
  *
- *   x:        bf16 bits [M][H]
+ *   x:        bf16 bits [M][H] (x_is_f16 = 0) or fp16 bits (x_is_f16 = 1)
  *   sel:      int32 [M][topk] global expert ids (< E)
  *   rw:       float [M][topk] routing weights (0 = inactive slot)
  *   ptrs:     host pointers, 9 per expert in the reference handle order
@@ -309,7 +309,7 @@ void eo_expert(const double* x, int M, int H, int I, int Ho,
  * Order of the sum: routed slots k = 0..topk-1 in order, then the shared expert
  * (exl3_moe_coop_kernel.cuh:906-949, model.py:498).
  */
-int eo_moe_forward(const uint16_t* x, int M, int H, int I, int topk, int E,
+int eo_moe_forward(const uint16_t* x, int x_is_f16, int M, int H, int I, int topk, int E,
                    const int32_t* sel, const float* rw, const void* const* ptrs, int K,
                    const void* const* sh_ptrs, int sh_I, int sh_K,
                    double limit, float* out_f32, uint16_t* out_bf16, int threads)
@@ -321,7 +321,7 @@ int eo_moe_forward(const uint16_t* x, int M, int H, int I, int topk, int E,
 #endif
     double* xd = (double*) malloc(sizeof(double) * (size_t) M * H);
     double* acc = (double*) calloc((size_t) M * H, sizeof(double));
-    for (size_t i = 0; i < (size_t) M * H; ++i) xd[i] = eo_bf16_to_f32(x[i]);
+    for (size_t i = 0; i < (size_t) M * H; ++i) xd[i] = x_is_f16 ? F16(x[i]) : eo_bf16_to_f32(x[i]);
 
     uint16_t* wg = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) H * (I > sh_I ? I : sh_I));
     uint16_t* wu = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) H * (I > sh_I ? I : sh_I));

@@ -60,7 +60,7 @@ def lib():
         L.eo_act.restype = dbl
         L.eo_act.argtypes = [dbl, dbl, dbl, i32]
         L.eo_moe_forward.restype = i32
-        L.eo_moe_forward.argtypes = [vp, i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, i32, i32,
+        L.eo_moe_forward.argtypes = [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, i32, i32,
                                      dbl, vp, vp, i32]
         _lib = L
     return _lib
@@ -255,11 +255,12 @@ def expert_offsets(sel: np.ndarray, rw: np.ndarray | None, n_experts: int) -> np
 # Full MoE layer from host-resident EXL3 experts
 
 
-def moe_forward(x_bf16: np.ndarray, sel: np.ndarray, rw: np.ndarray, layer, threads: int = 0,
-                with_shared: bool = True) -> np.ndarray:
-    """Routed experts + shared expert, float32 [M, H]. `layer` is an ExpertLayer in host memory."""
+def moe_forward(x_bits: np.ndarray, sel: np.ndarray, rw: np.ndarray, layer, threads: int = 0,
+                with_shared: bool = True, x_is_f16: bool = False) -> np.ndarray:
+    """Routed experts + shared expert, float32 [M, H]. `layer` is an ExpertLayer in host memory;
+    x_bits are bf16 bit patterns (or fp16 with x_is_f16)."""
     cfg = layer.cfg
-    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
     M, H = x.shape
     sel32 = np.ascontiguousarray(sel, dtype=np.int32)
     rw32 = np.ascontiguousarray(rw, dtype=np.float32)
@@ -269,7 +270,7 @@ def moe_forward(x_bf16: np.ndarray, sel: np.ndarray, rw: np.ndarray, layer, thre
     if with_shared and layer.shared is not None:
         sh = np.ascontiguousarray(layer.shared.numpy(), dtype=np.int64)
     out = np.empty((M, H), dtype=np.float32)
-    st = lib().eo_moe_forward(_ptr(x), M, H, cfg.inter, cfg.topk, cfg.n_experts, _ptr(sel32), _ptr(rw32),
+    st = lib().eo_moe_forward(_ptr(x), int(x_is_f16), M, H, cfg.inter, cfg.topk, cfg.n_experts, _ptr(sel32), _ptr(rw32),
                               _ptr(ptrs), cfg.bits, None if sh is None else _ptr(sh),
                               cfg.shared_inter if sh is not None else 0, cfg.shared_bits,
                               float(cfg.swiglu_limit), _ptr(out), None, int(threads))

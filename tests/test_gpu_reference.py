@@ -1,0 +1,127 @@
+"""The eva_b200 kernels against the reference's OWN GPU kernels on the same B200 and inputs.
+
+oracle/_ref/libref_coop.so is compiled from the reference checkout by oracle/build_ref.py (the
+vendored ExLlamaV3 dq_dispatch decoder and MoE coop rot/A/B kernels, launched by our harness). The
+tests skip when that library was not built. Needs a GPU: -m gpu.
+"""
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from eva_b200 import _lib
+from eva_b200 import config as C
+from eva_b200.experts import make_layer
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+REF = Path(__file__).resolve().parent.parent / "oracle" / "_ref" / "libref_coop.so"
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not REF.exists():
+        pytest.skip("oracle/_ref/libref_coop.so not built (needs the reference checkout)")
+    L = ctypes.CDLL(str(REF))
+    vp, i32 = ctypes.c_void_p, ctypes.c_int
+    L.ref_dequant.restype = i32
+    L.ref_dequant.argtypes = [vp, i32, i32, i32, vp, vp]
+    L.ref_coop_ctr_len.restype = ctypes.c_longlong
+    L.ref_coop_ctr_len.argtypes = [i32, i32, i32, i32]
+    L.ref_coop_run.restype = i32
+    L.ref_coop_run.argtypes = [vp, vp, vp, i32, i32, i32, i32, ctypes.POINTER(vp), i32, vp, vp, vp, vp, vp, vp,
+                               vp, i32, vp, i32, ctypes.c_float, vp]
+    return L
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+@pytest.mark.parametrize("K", [2, 3, 4])
+def test_dequant_bit_exact_vs_reference_kernel(ref, oracle, K):
+    """The reference's dq_dispatch<K, mul1> == our CPU decoder == our GPU decoder, bit for bit."""
+    fin, fout = 512, 384
+    g = torch.Generator().manual_seed(100 + K)
+    tr = torch.randint(-32768, 32768, (fin // 16, fout // 16, 16 * K), generator=g, dtype=torch.int32).to(torch.int16)
+    trd = tr.to(DEV)
+    wr = torch.empty(fin, fout, dtype=torch.int16, device=DEV)
+    we = torch.empty(fin, fout, dtype=torch.int16, device=DEV)
+    assert ref.ref_dequant(trd.data_ptr(), fin, fout, K, wr.data_ptr(), stream()) == 0
+    lib = _lib.load()
+    _lib.check(lib.eva_exl3_dequant(trd.data_ptr(), fin, fout, K, we.data_ptr(), stream()), "dequant")
+    torch.cuda.synchronize()
+    w_ref = wr.cpu().numpy().view(np.uint16)
+    assert np.array_equal(w_ref, oracle.dequant(tr.numpy(), K))
+    assert np.array_equal(we.cpu().numpy().view(np.uint16), w_ref)
+
+
+def ref_coop(ref, layer_d, x16, sel, rw16, K, limit, capacity=None):
+    cfg = layer_d.cfg
+    M, topk, H, I = x16.shape[0], sel.shape[1], cfg.hidden, cfg.inter
+    cap = capacity or M
+    slots = cap * topk
+    o = dict(device=DEV)
+    had_g = torch.empty(slots, H, dtype=torch.float16, **o)
+    had_u = torch.empty_like(had_g)
+    gu_g = torch.empty(slots, I, dtype=torch.float16, **o)
+    gu_u = torch.empty_like(gu_g)
+    act = torch.empty_like(gu_g)
+    d_out = torch.empty(slots, H, dtype=torch.float32, **o)
+    ctr = torch.zeros(ref.ref_coop_ctr_len(cap, topk, I, H), dtype=torch.int32, **o)
+    out = torch.empty(cap, H, dtype=torch.float32, **o)
+    tabs = (ctypes.c_void_p * 9)(*[t.data_ptr() for t in layer_d.packed.unbind(0)])
+    rc = ref.ref_coop_run(x16.data_ptr(), sel.data_ptr(), rw16.data_ptr(), M, topk, H, I, tabs, cfg.n_experts,
+                          had_g.data_ptr(), had_u.data_ptr(), gu_g.data_ptr(), gu_u.data_ptr(), act.data_ptr(),
+                          d_out.data_ptr(), ctr.data_ptr(), cap, out.data_ptr(), K, float(limit), stream())
+    assert rc == 0
+    return out[:M]
+
+
+def eva_routed(layer_d, x16, sel, rw, limit):
+    from eva_b200.runner import EvaMoERunner
+    cfg = layer_d.cfg
+    r = EvaMoERunner(DEV, topk=cfg.topk, hidden=cfg.hidden, inter=cfg.inter, max_rows=x16.shape[0],
+                     n_experts=cfg.n_experts)
+    return r.run(x16, sel, rw, tuple(layer_d.packed.unbind(0)), cfg.bits, limit)
+
+
+CASES = [
+    C.MoEConfig("small", hidden=512, inter=256, n_experts=16, topk=6, router="sqrtsoftplus", bits=3),
+    C.MoEConfig("v2l-routed", hidden=2048, inter=1408, n_experts=64, topk=6, router="softmax", bits=4),
+    C.MoEConfig("ref-native-routed", hidden=5120, inter=2304, n_experts=384, topk=6, router="sqrtsoftplus",
+                bits=3, swiglu_limit=10.0),
+    C.MoEConfig("v3-routed-k2", hidden=7168, inter=2048, n_experts=256, topk=8, router="sigmoid", bits=2),
+]
+
+
+@pytest.mark.parametrize("cfg", CASES, ids=lambda c: c.name)
+@pytest.mark.parametrize("M", [1, 5])
+def test_moe_matches_reference_kernels(ref, oracle, cfg, M):
+    """Same x, routes, Half route weights and expert tables through the reference's coop kernels and
+    through eva_moe_experts; both against the FP64 oracle. The reference accumulates in fp16, so it
+    sits ~1e-3 from the oracle; ours sits closer."""
+    layer_d = make_layer(cfg, DEV, seed=M)
+    rng = np.random.default_rng(M)
+    sel = np.stack([rng.choice(cfg.n_experts, cfg.topk, replace=False) for _ in range(M)]).astype(np.int64)
+    rw = (rng.random((M, cfg.topk)) + 0.1).astype(np.float32)
+    x16 = torch.randn(M, cfg.hidden, generator=torch.Generator().manual_seed(M)).to(torch.float16).to(DEV)
+    seld = torch.tensor(sel, device=DEV)
+    rw16 = torch.tensor(rw, device=DEV).half()
+    y_ref = ref_coop(ref, layer_d, x16, seld, rw16, cfg.bits, cfg.swiglu_limit).cpu().numpy()
+    y_eva = eva_routed(layer_d, x16, seld, rw16, cfg.swiglu_limit).cpu().numpy()
+    torch.cuda.synchronize()
+    # oracle on the selected experts only (host copy of the few records used)
+    host = layer_d.host_copy()
+    ref64 = oracle.moe_forward(x16.cpu().view(torch.int16).numpy().view(np.uint16), sel,
+                               rw16.float().cpu().numpy(), host, with_shared=False, x_is_f16=True)
+    scale = np.abs(ref64).max()
+    e_ref = np.abs(y_ref - ref64).max() / scale
+    e_eva = np.abs(y_eva - ref64).max() / scale
+    e_cross = np.abs(y_eva - y_ref).max() / scale
+    cos = float((y_eva.ravel() @ y_ref.ravel()) / (np.linalg.norm(y_eva) * np.linalg.norm(y_ref)))
+    print(f"{cfg.name} M={M}: ref-vs-oracle {e_ref:.2e}, eva-vs-oracle {e_eva:.2e}, eva-vs-ref {e_cross:.2e}, cos {cos:.7f}")
+    assert e_cross <= 2e-2 and cos >= 0.9999
+    assert e_eva <= 3e-3
