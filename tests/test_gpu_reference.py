@@ -125,3 +125,37 @@ def test_moe_matches_reference_kernels(ref, oracle, cfg, M):
     print(f"{cfg.name} M={M}: ref-vs-oracle {e_ref:.2e}, eva-vs-oracle {e_eva:.2e}, eva-vs-ref {e_cross:.2e}, cos {cos:.7f}")
     assert e_cross <= 2e-2 and cos >= 0.9999
     assert e_eva <= 3e-3
+
+
+def test_speed_vs_reference_kernels(ref, capsys):
+    """Routed experts of the DeepSeek-V3 decode step (batch 8, K3, 4.24 GB of experts): the reference's
+    prepare/rot/A/B launches vs eva_moe_experts, same routes, CUDA events, a different batch every
+    iteration (working set larger than L2). Prints both times; asserts only that both ran."""
+    cfg = C.V3.with_(shared_inter=0)
+    layer_d = make_layer(cfg, DEV, seed=0)
+    M, iters = 8, 20
+    rng = np.random.default_rng(0)
+    sels = [torch.tensor(np.stack([rng.choice(cfg.n_experts, cfg.topk, replace=False) for _ in range(M)]),
+                         device=DEV) for _ in range(iters + 3)]
+    rw16 = torch.full((M, cfg.topk), 0.125, device=DEV).half()
+    xs = [torch.randn(M, cfg.hidden, device=DEV).half() for _ in range(iters + 3)]
+    from eva_b200.runner import EvaMoERunner
+    r = EvaMoERunner(DEV, topk=cfg.topk, hidden=cfg.hidden, inter=cfg.inter, max_rows=M, n_experts=cfg.n_experts)
+    times = {}
+    for name in ("reference", "eva"):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        for i in range(iters + 3):
+            if i == 3:
+                torch.cuda.synchronize()
+                ev[0].record()
+            if name == "reference":
+                ref_coop(ref, layer_d, xs[i], sels[i], rw16, cfg.bits, 0.0)
+            else:
+                r.run(xs[i], sels[i], rw16, tuple(layer_d.packed.unbind(0)), cfg.bits, 0.0, check_bounds=False)
+        ev[1].record()
+        torch.cuda.synchronize()
+        times[name] = ev[0].elapsed_time(ev[1]) / iters
+    with capsys.disabled():
+        print(f"\nV3 decode routed experts, batch {M}, K3: reference {times['reference']:.3f} ms/step, "
+              f"eva {times['eva']:.3f} ms/step, speed-up {times['reference'] / times['eva']:.2f}x")
+    assert times["reference"] > 0 and times["eva"] > 0
