@@ -19,7 +19,8 @@ ACT_CLAMP_AFTER, ACT_CLAMP_BEFORE = 0, 1
 # every symbol include/eva_moe.h declares
 EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_status", "eva_moe_route",
            "eva_moe_topk", "eva_moe_permute", "eva_moe_experts", "eva_moe_forward", "eva_exl3_dequant",
-           "eva_moe_arch")
+           "eva_moe_arch", "eva_moe_experts_noalloc")
+NOALLOC_SCRATCH_BYTES = 16 << 20
 
 
 class EvaMoeShape(ctypes.Structure):
@@ -74,6 +75,8 @@ def load(build_if_missing: bool = True):
                                   vp, vp, vp, vp]
     L.eva_exl3_dequant.restype = ctypes.c_int
     L.eva_exl3_dequant.argtypes = [vp, i32, i32, i32, vp, vp]
+    L.eva_moe_experts_noalloc.restype = ctypes.c_int
+    L.eva_moe_experts_noalloc.argtypes = [shp, vp, i32, i32, vp, i32, vp, P(vp), P(ctypes.c_int64), vp, vp, vp, vp]
     L.eva_moe_arch.restype = i32
     L.eva_moe_arch.argtypes = []
     _lib = L

@@ -10,7 +10,7 @@ namespace eva {
 
 static size_t up256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
-WsLayout ws_layout(const EvaMoeShape& s, int max_rows)
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split)
 {
     WsLayout L{};
     L.max_rows = max_rows;
@@ -44,8 +44,9 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows)
     L.xrot = take(2 * St * H * 2);
     L.act = take(St * L.imax * 2);
     L.dpart = take(St * H * 4);
-    const size_t pa = std::min<size_t>(PARTA_ITEMS, R * L.nchA * 4);
+    const size_t pa = allow_split ? std::min<size_t>(PARTA_ITEMS, R * L.nchA * 4) : 0;
     L.partA = take(pa * 2 * RUN_ROWS * 128 * 4);
+    L.max_split = allow_split ? 4 : 1;
     L.total = o;
     return L;
 }
@@ -177,9 +178,14 @@ int eva_moe_permute(const EvaMoeShape* shape, const void* sel, int32_t sel_is_i6
     return cuda_status(launch_permute(pa, static_cast<cudaStream_t>(stream)));
 }
 
-static int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
-                        int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
-                        void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st)
+}  // extern "C"
+
+namespace eva {
+
+int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
+                 int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
+                 void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,
+                 bool allow_split)
 {
     if (!shape_ok(shape) || M < 0 || !x || !sel || !rw || !tables || !workspace) return EVA_ERR_INVALID;
     if (!out_f32 && !out_bf16) return EVA_ERR_INVALID;
@@ -191,7 +197,7 @@ static int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf
         for (int i = 0; i < 9; ++i)
             if (shared[i] == 0 || (shared[i] & 15)) return EVA_ERR_INVALID;   // bulk copies need 16 B
     if (M == 0) return EVA_OK;
-    const WsLayout L = ws_layout(*shape, M);
+    const WsLayout L = ws_layout(*shape, M, allow_split);
     if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     PermuteArgs pa;
@@ -228,6 +234,10 @@ static int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf
     ea.out_bf16 = out_bf16;
     return cuda_status(launch_experts(ea, st));
 }
+
+}  // namespace eva
+
+extern "C" {
 
 int eva_moe_experts(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
                     int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,

@@ -548,7 +548,7 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
     const int r_max = a.M * s.topk + (p.has_shared ? (a.M + RUN_ROWS - 1) / RUN_ROWS : 0);
     const int items_a = r_max * (L.imax / 128);
     int split = 1;
-    while (split < 4 && items_a * split * 2 <= 2 * sms && items_a * split * 2 <= PARTA_ITEMS) split *= 2;
+    while (split < L.max_split && items_a * split * 2 <= 2 * sms && items_a * split * 2 <= PARTA_ITEMS) split *= 2;
     p.split_a = split;
 
     static int configured_device = -1;

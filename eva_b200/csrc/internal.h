@@ -18,9 +18,11 @@ struct WsLayout {
     int max_rows, S, R, imax, nchA, nchH, ks_router;
     size_t status, counters, n_counters, runs, run_expert, estart, slot_act, tok_expect;
     size_t logits, idx, w, xrot, act, dpart, partA, total;
+    int max_split;   // largest gate/up k-split the partial buffer allows (1 = none)
 };
 
-WsLayout ws_layout(const EvaMoeShape& s, int max_rows);
+// allow_split = false leaves out the split-k partial buffer (gate/up items are then never split).
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split = true);
 
 // Counter block layout inside `counters` (int32 indices).
 struct CtrLayout {
@@ -67,6 +69,12 @@ struct ExpertsArgs {
     void* out_bf16;
 };
 cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream);
+
+// Permutation + fused experts on a caller-provided workspace laid out by ws_layout(shape, M, allow_split).
+int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
+                 int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
+                 void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,
+                 bool allow_split = true);
 
 cudaError_t launch_dequant(const void* trellis, int in, int out, int K, uint16_t* w, cudaStream_t stream);
 

@@ -124,6 +124,31 @@ int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, 
 int eva_exl3_dequant(const void* trellis, int32_t in_features, int32_t out_features, int32_t bits,
                      uint16_t* w_out, void* stream);
 
+/* Size of the fixed device scratch behind eva_moe_experts_noalloc: 16 MiB, reserved on every GPU that
+ * loads this library until the process exits. */
+#define EVA_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* eva_moe_experts without a workspace: it allocates nothing. No counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory: a serving runtime that has already reserved the
+ * GPU's memory in its own pool (a cudaMalloc would fail or fragment it), a plugin host that hands
+ * over input and output buffers but no allocator, or a latency-critical loop that must not call
+ * cudaMalloc because it can synchronise the device. The caller passes inputs and outputs exactly as
+ * for eva_moe_experts; the scratch is a file-scope device array of EVA_NOALLOC_SCRATCH_BYTES.
+ *   - Calls whose scratch would exceed that size are rejected with EVA_ERR_WORKSPACE (for the
+ *     DeepSeek-V3 shape this allows up to 29 tokens per call, DeepSeek-V2-Lite 108).
+ *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress)
+ *     with that device current; make that first call before any stream capture.
+ *   - All calls share the one array, which keeps the previous call's contents. Each call clears
+ *     what must start at zero on its own stream. Calls that overlap on the GPU race on the array:
+ *     issue them in order on one stream.
+ *   - status_out (device int32, may be NULL) receives the call's EVA_STATUS_* bits.
+ * No cudaMalloc, cudaFree or other allocating routine is called. */
+int eva_moe_experts_noalloc(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
+                            const void* sel, int32_t sel_is_i64, const float* rw,
+                            const int64_t* const* tables, const int64_t* shared,
+                            float* out_f32, void* out_bf16, int32_t* status_out, void* stream);
+
 /* Library identification: sm arch the kernels were built for (100 for sm_100a). */
 int32_t eva_moe_arch(void);
 
