@@ -73,6 +73,15 @@ class ClockSampler:
         self.proc = None
         self.lines = []
 
+    def wait_first(self, timeout=3.0):
+        t_end = time.time() + timeout
+        while not self.lines and time.time() < t_end:
+            time.sleep(0.02)
+
+    def mark(self):
+        """Index of the next sample: samples from here on fall in the region being measured."""
+        return len(self.lines)
+
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
@@ -96,10 +105,10 @@ class ClockSampler:
             except Exception:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, start=0, end=None):
         sm, smax, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[start:end]:
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -236,6 +245,8 @@ def main():
         if ev is not None:
             ev[1].record(stream)
 
+    clocks = ClockSampler(local).__enter__()
+    clocks.wait_first()
     for i in range(warmup):
         step(i)
     torch.cuda.synchronize()
@@ -245,17 +256,19 @@ def main():
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        t0.record(stream)
-        for i in range(steps):
-            step(warmup + i, evs[i])
-        t1.record(stream)
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    c_start = clocks.mark()
+    t0.record(stream)
+    for i in range(steps):
+        step(warmup + i, evs[i])
+    t1.record(stream)
+    torch.cuda.synchronize()
+    time.sleep(0.06)   # let the sampler report the end of the region
+    c_end = clocks.mark()
+    if world > 1:
+        dist.barrier()
     ms_total = t0.elapsed_time(t1)
     exp_ms = [a.elapsed_time(b) for a, b in evs]
     if world > 1:
@@ -289,6 +302,12 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+
+    clocks.__exit__(None, None, None)
+    clock_summary = clocks.summary(c_start, c_end)
+    if not clock_summary["samples"]:
+        clock_summary = dict(clocks.summary(), note="timed region shorter than the 50 ms sampling period; "
+                                                    "samples from warm-up through e2e")
 
     # ---- roofline of the fused experts launch -------------------------------------------------
     U = [len(np.unique(idx_host[warmup + i])) for i in range(steps)]
@@ -341,7 +360,7 @@ def main():
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": M * cfg.hidden * 2,
                 "d2h_bytes_per_step": M * cfg.hidden * 2},
         "gpu_launches": 4 * steps,
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
         "device_status": st,
     }
     if rank == 0:

@@ -41,9 +41,15 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split)
     L.logits = take(lrows * E * 4);
     L.idx = take(M * s.topk * 4);
     L.w = take(M * s.topk * 4);
-    L.xrot = take(2 * St * H * 2);
-    L.act = take(St * L.imax * 2);
+    // fragment-layout copies of the GEMV inputs: rows padded by one stage (32 k-tile rows = 512
+    // elements) so the last stage's reads past the end of a row stay inside the buffer
+    L.hpad = (s.hidden + 511) / 512 * 512 + 512;
+    L.ipad = (L.imax + 511) / 512 * 512 + 512;
+    L.xrot = take(2 * St * static_cast<size_t>(L.hpad) * 2);
+    L.act = take(St * static_cast<size_t>(L.ipad) * 2);
     L.dpart = take(St * H * 4);
+    L.xsum = take(2 * St * L.nchH * 4);
+    L.asum = take(St * L.nchA * 4);
     const size_t pa = allow_split ? std::min<size_t>(PARTA_ITEMS, R * L.nchA * 4) : 0;
     L.partA = take(pa * 2 * RUN_ROWS * 128 * 4);
     L.max_split = allow_split ? 4 : 1;

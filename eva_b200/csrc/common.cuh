@@ -112,6 +112,17 @@ __device__ __forceinline__ bool wait_geq(const int* p, int target, int* status)
     return true;
 }
 
+// Ampere-style async copy of 8 bytes global -> shared (L1-cached; only for data not written during
+// the kernel), with group commit / wait.
+__device__ __forceinline__ void cp_async8(void* dst, const void* src)
+{
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 __device__ __forceinline__ void named_sync(int id, int threads)
 {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -201,8 +212,9 @@ __device__ __forceinline__ void load4_x(const void* x, size_t off, int is_bf16, 
 // A 16x16 tile holds 256 K-bit codes in 8K 32-bit words, bits MSB-first through the words. The
 // 16-bit state of position p is the window ending at bit (p+1)K, circular modulo 256K. State ->
 // weight: byte sum of state * 0x83DCD12D added to the fp16 pattern of 1024.0 (exact fp16 1024 +
-// sum), then one fp16 FMA with the constants 0x1eee, 0xc931 (codebook format of the reference's
-// vendored ExLlamaV3 headers; see DESIGN.md "format constants").
+// sum), then one fp16 FMA with the constants 0x1eee, 0xc931. These constants define the EXL3 mul1
+// codebook (ExLlamaV3, vendored by the reference at runtime/ds41/csrc/moe_coop2048/vendor/quant/
+// codebook.cuh:86-99); the stored weights only mean anything under them.
 //
 // Lane l decodes positions 8l..8l+7. With p = 8l + j the position is weight (k, n) of the tile:
 // n = l/4 + 8(j/4), k = 2(l%4) + (j%2) + 8((j/2)%2). That is exactly the A fragment of
@@ -222,22 +234,101 @@ __device__ __forceinline__ uint32_t mul1_pair(uint32_t s0, uint32_t s1)
     return *reinterpret_cast<const uint32_t*>(&r);
 }
 
-// The 8 states of lane `lane` from the tile's words (smem or global).
+// Per-lane decode constants of a K-bit tile: the two words that hold the lane's 8 windows (wrap
+// resolved) and the bit offset of the first window inside them.
+struct LaneDec {
+    int w0, w1, off;
+};
+
 template <int K>
-__device__ __forceinline__ void lane_states(const uint32_t* tile, int lane, uint32_t (&st)[8])
+__device__ __forceinline__ LaneDec lane_dec(int lane)
 {
     constexpr int NB = 256 * K, NW = 8 * K;
     int start = (8 * lane + 1) * K - 16;
     if (start < 0) start += NB;
-    const int w0 = start >> 5, off = start & 31;
-    const uint32_t hi = tile[w0];
-    const uint32_t lo = tile[(w0 + 1 == NW) ? 0 : w0 + 1];
-    const uint64_t v = (static_cast<uint64_t>(hi) << 32) | lo;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) st[j] = static_cast<uint32_t>(v >> (48 - off - j * K)) & 0xffffu;
+    LaneDec d;
+    d.w0 = start >> 5;
+    d.w1 = d.w0 + 1 == NW ? 0 : d.w0 + 1;
+    d.off = start & 31;
+    return d;
 }
 
-// A fragment (4 x half2) of lane `lane` for one tile.
+// The 8 states of one tile for a lane: the 16-bit windows ending at bits (8 lane + j + 1) K lie
+// within two consecutive words (16 + 7K <= 44 bits, offset <= 27 for K <= 4).
+template <int K>
+__device__ __forceinline__ void lane_states(const uint32_t* tile, const LaneDec& d, uint32_t (&st)[8])
+{
+    const uint64_t v = (static_cast<uint64_t>(tile[d.w0]) << 32) | tile[d.w1];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) st[j] = static_cast<uint32_t>(v >> (48 - d.off - j * K)) & 0xffffu;
+}
+
+template <int K>
+__device__ __forceinline__ void lane_states(const uint32_t* tile, int lane, uint32_t (&st)[8])
+{
+    lane_states<K>(tile, lane_dec<K>(lane), st);
+}
+
+// Raw-codebook decode for the GEMV (decode_raw): the MMA takes h = 1024 + bytesum as an exact fp16
+// value and the affine map w = c0 h + c1 (c0, c1 = fp16 0x1eee, 0xc931) is applied to the sums:
+// sum_k x_k w_k = c0 sum_k x_k h_k + c1 sum_k x_k. This drops the per-weight fp16 FMA; the weights
+// used are c0 h + c1 before their single fp16 rounding (|difference| <= half an fp16 ulp).
+constexpr float CB_C0 = 0.00676727294921875f;   // fp16 0x1eee
+constexpr float CB_C1 = -10.3828125f;           // fp16 0xc931
+
+// The two groups of 4 windows (0-3 and 4-7) each span 16 + 3K <= 28 bits, so one funnel shift
+// (amount < 32) of the two words around the group's end puts its last window in bits 0-15 and
+// the others K, 2K, 3K bits higher.
+struct LaneGrp {
+    int b0, b1, a0, a1;   // word indices (wrap resolved) of group 0-3 (b) and 4-7 (a)
+    int shb, sha;
+};
+
+template <int K>
+__device__ __forceinline__ LaneGrp lane_grp(int lane)
+{
+    constexpr int NW = 8 * K;
+    LaneGrp g;
+    const int eb = (8 * lane + 4) * K, ea = (8 * lane + 8) * K;   // end bits of windows 3 and 7
+    const int wb = (eb + 31) / 32 - 2, wa = (ea + 31) / 32 - 2;
+    g.shb = 32 * (wb + 2) - eb;
+    g.sha = 32 * (wa + 2) - ea;
+    g.b0 = wb < 0 ? wb + NW : wb;
+    g.a0 = wa < 0 ? wa + NW : wa;
+    g.b1 = g.b0 + 1 == NW ? 0 : g.b0 + 1;
+    g.a1 = g.a0 + 1 == NW ? 0 : g.a0 + 1;
+    return g;
+}
+
+template <int K>
+__device__ __forceinline__ void decode_raw(const uint32_t* tile, const LaneGrp& g, uint32_t (&a)[4])
+{
+    const uint32_t wb = __funnelshift_r(tile[g.b1], tile[g.b0], g.shb);
+    const uint32_t wa = __funnelshift_r(tile[g.a1], tile[g.a0], g.sha);
+    uint32_t h[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        h[3 - j] = mul1_sum((wb >> (j * K)) & 0xffffu);
+        h[7 - j] = mul1_sum((wa >> (j * K)) & 0xffffu);
+    }
+    a[0] = __byte_perm(h[0], h[1], 0x5410);
+    a[1] = __byte_perm(h[4], h[5], 0x5410);
+    a[2] = __byte_perm(h[2], h[3], 0x5410);
+    a[3] = __byte_perm(h[6], h[7], 0x5410);
+}
+
+// A fragment (4 x half2) of one tile for a lane: exact fp16 weights.
+template <int K>
+__device__ __forceinline__ void decode_afrag(const uint32_t* tile, const LaneDec& d, uint32_t (&a)[4])
+{
+    uint32_t st[8];
+    lane_states<K>(tile, d, st);
+    a[0] = mul1_pair(st[0], st[1]);
+    a[1] = mul1_pair(st[4], st[5]);
+    a[2] = mul1_pair(st[2], st[3]);
+    a[3] = mul1_pair(st[6], st[7]);
+}
+
 template <int K>
 __device__ __forceinline__ void decode_afrag(const uint32_t* tile, int lane, uint32_t (&a)[4])
 {

@@ -12,9 +12,14 @@
 // which were claimed earlier by running CTAs, so the schedule cannot deadlock.
 //
 // Per CTA: 1 producer warp streams the item's trellis rows with 1-D bulk copies (TMA, no
-// multicast) into an 8-stage shared-memory ring; 16 consumer warps decode the codes of one 16-row
-// k slice each and run mma.m16n8k16 with the weights as the 16 x 16 A operand (rows = output
-// columns) and up to 8 tokens as the B operand, accumulating in fp32.
+// multicast) into a 4-stage shared-memory ring (32 k-tile rows x 128 columns per stage); 16
+// consumer warps each decode 4 rows x 4 tiles per stage in registers and run mma.m16n8k16 with
+// the weights as the 16 x 16 A operand (rows = output columns) and up to 8 tokens as the B
+// operand, accumulating in fp32. The MMA takes the raw codebook values h = 1024 + bytesum and the
+// affine map of the codebook is applied to the sums (see decode_raw). Each warp follows the item
+// sequence on its own; the only CTA-wide barriers are the cross-warp k reduction at the end of a
+// projection, the rotation items and the split-k hand-off. The epilogue of a run row is done by
+// one warp while the others go on to the next item.
 //
 // Reference behaviour (paths within Findddx/eva, runtime/ds41/csrc/moe_coop2048/vendor/quant/):
 //   exl3_moe_coop_kernel.cuh:634-671 (rotation), :680-809 (gate/up GEMV + epilogue),
@@ -28,17 +33,17 @@ namespace eva {
 
 constexpr int NCW = 16;                    // consumer warps
 constexpr int THREADS = (NCW + 1) * 32;    // + producer warp
-constexpr int NSTAGE = 8;
-constexpr int STAGE_KT = 16;               // k-tile rows per stage (one per consumer warp)
+constexpr int NSTAGE = 4;
+constexpr int STAGE_KT = 32;               // k-tile rows per stage (4 per consumer warp pair)
 constexpr int NT = 8;                      // 16-column tiles per item (128 output columns)
 constexpr int STAGE_BYTES = STAGE_KT * NT * 32 * 4;   // sized for K = 4
-constexpr int RED_FLOATS = NCW * NT * 4 * 32;
+constexpr int RED_FLOATS = NCW * 4 * 4 * 32;  // [warp][tile][c][lane]
 constexpr int RES_FLOATS = 2 * RUN_ROWS * 128;
 constexpr size_t SMEM_BYTES = static_cast<size_t>(NSTAGE) * STAGE_BYTES + RED_FLOATS * 4 + RES_FLOATS * 4 + 1024;
 
 struct KParams {
     // shape
-    int M, H, I, topk, n_local, K, I_sh, K_sh, has_shared, S_cap, imax, split_a;
+    int M, H, I, topk, n_local, K, I_sh, K_sh, has_shared, S_cap, imax, split_a, hpad, ipad;
     int act_routed, act_shared;
     float limit;
     // inputs
@@ -52,10 +57,12 @@ struct KParams {
     const int* slot_act;
     const int* tok_expect;
     // scratch
-    __half* xrot;             // [2][S_tot][H]
-    __half* act;              // [S_tot][imax]
+    __half* xrot;             // [2][S_tot][hpad] rotated gate/up inputs, fragment layout
+    __half* act;              // [S_tot][ipad] down inputs, fragment layout
     float* dpart;             // [S_tot][H]
     float* partA;             // [PARTA_ITEMS][2][8][128]
+    float* xsum;              // [2][S_tot][H/128] sums of the fp16 rotated inputs per 128 chunk
+    float* asum;              // [S_tot][imax/128] sums of the fp16 down inputs per 128 chunk
     int* ctr_work;
     int* ctr0;
     int* ctrA;
@@ -178,54 +185,95 @@ __device__ __forceinline__ int total_items(const KParams& p)
 }
 
 // ---------------------------------------------------------------------------------------------
-// Consumer: one stage of one projection. Warp w handles k-tile row kt0 + w (if valid), all 8 tiles.
+// Fragment layout of a GEMV input row: every 64 elements (4 k-tile rows) form one 128-byte block in
+// which lane q of a token's lane group finds the B fragments of the 4 rows contiguously:
+// half offset (q * 4 + r) * 4 + w * 2 + sub holds element k = 16 (4 b + r) + 8 w + 2 q + sub.
+__device__ __forceinline__ int frag_offset(int k)
+{
+    const int b = k >> 6, r = (k >> 4) & 3, k16 = k & 15;
+    const int q = (k16 & 7) >> 1, w = k16 >> 3, sub = k16 & 1;
+    return b * 64 + (q * 4 + r) * 4 + w * 2 + sub;
+}
+
+// Store 4 consecutive elements k0..k0+3 (k0 % 4 == 0) as fp16 in fragment layout: two 4-byte stores.
+__device__ __forceinline__ void store4_frag(__half* row, int k0, const float (&v)[4])
+{
+    const __half2 a = __floats2half2_rn(v[0], v[1]);
+    const __half2 b = __floats2half2_rn(v[2], v[3]);
+    *reinterpret_cast<__half2*>(row + frag_offset(k0)) = a;
+    *reinterpret_cast<__half2*>(row + frag_offset(k0 + 2)) = b;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Consumers. A stage holds 32 k-tile rows x 8 tiles (128 output columns). Warp w takes k-tile rows
+// 4 (w / 2) .. 4 (w / 2) + 3 of the stage and tiles 4 (w % 2) .. 4 (w % 2) + 3, i.e. 16 tiles and
+// 16 fp32 accumulator registers; the eight warps of one column half split k and are summed at the
+// end of a projection.
+
+constexpr int WT = 4;   // tiles per warp per k-tile row
+constexpr int WR = 4;   // k-tile rows per warp per stage
+
+// B fragments of the 4 k-tile rows 4 g .. 4 g + 3 for lane `lane`: one 32-byte contiguous read
+// (row = fragment-layout input row of the lane's token).
+__device__ __forceinline__ void load_b4(const __half* row, int g, int lane, uint32_t (&b)[2 * WR])
+{
+    const uint4* p = reinterpret_cast<const uint4*>(row + g * 64 + (lane & 3) * 16);
+    const uint4 u0 = __ldcg(p), u1 = __ldcg(p + 1);
+    b[0] = u0.x; b[1] = u0.y; b[2] = u0.z; b[3] = u0.w;
+    b[4] = u1.x; b[5] = u1.y; b[6] = u1.z; b[7] = u1.w;
+}
 
 template <int K>
-__device__ __forceinline__ void gemv_stage(const uint32_t* buf, int nvalid, int warp, int lane, const __half* src,
-                                           int width, int kt0, const int* sh_slot, int nrows, float (&acc)[NT][4])
+__device__ __forceinline__ void gemv_row(const uint32_t* tiles, const LaneGrp& d, uint32_t b0, uint32_t b1,
+                                         float (&acc)[WT][4])
 {
-    if (warp >= nvalid) return;
-    const int kt = kt0 + warp;
-    const int t = lane >> 2, q = lane & 3;
-    uint32_t b0 = 0, b1 = 0;
-    if (t < nrows) {
-        const __half* a = src + static_cast<size_t>(sh_slot[t]) * width + kt * 16 + 2 * q;
-        b0 = __ldcg(reinterpret_cast<const unsigned int*>(a));
-        b1 = __ldcg(reinterpret_cast<const unsigned int*>(a + 8));
-    }
-    const uint32_t* row = buf + warp * NT * 8 * K;
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
+    for (int t = 0; t < WT; ++t) {
         uint32_t a[4];
-        decode_afrag<K>(row + nt * 8 * K, lane, a);
-        mma_16816(acc[nt], a, b0, b1);
+        decode_raw<K>(tiles + t * 8 * K, d, a);
+        mma_16816(acc[t], a, b0, b1);
     }
 }
 
-// Cross-warp reduction of the 16 k-split accumulators into res[tok][col] (natural layout).
-__device__ __forceinline__ void reduce_acc(float (&acc)[NT][4], float* red, float* res, int tid, int warp, int lane)
+// Sum of the 8 k-split accumulators of each column half into res[tok][col] (natural layout).
+__device__ __forceinline__ void reduce_acc(float (&acc)[WT][4], float* red, float* res, int tid, int warp, int lane)
 {
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int t = 0; t < WT; ++t)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) red[((warp * NT + nt) * 4 + c) * 32 + lane] = acc[nt][c];
+        for (int c = 0; c < 4; ++c) red[((warp * WT + t) * 4 + c) * 32 + lane] = acc[t][c];
     named_sync(1, NCW * 32);
-    for (int v = tid; v < NT * 4 * 32; v += NCW * 32) {
-        float s = 0.0f;
+    for (int v = tid; v < 2 * WT * 4 * 32; v += NCW * 32) {
+        const int half = v >> 9, r = v & 511;        // r = (t * 4 + c) * 32 + lane
+        float sum = 0.0f;
 #pragma unroll
-        for (int w = 0; w < NCW; ++w) s += red[w * NT * 4 * 32 + v];
-        const int l = v & 31, c = (v >> 5) & 3, nt = v >> 7;
-        const int col = nt * 16 + (l >> 2) + 8 * (c >> 1);
+        for (int pr = 0; pr < NCW / 2; ++pr) sum += red[(2 * pr + half) * WT * 4 * 32 + r];
+        const int l = r & 31, c = (r >> 5) & 3, t = r >> 7;
+        const int col = (half * WT + t) * 16 + (l >> 2) + 8 * (c >> 1);
         const int tok = 2 * (l & 3) + (c & 1);
-        res[tok * 128 + col] = s;
+        res[tok * 128 + col] = CB_C0 * sum;
     }
     named_sync(1, NCW * 32);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int t = 0; t < WT; ++t)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+        for (int c = 0; c < 4; ++c) acc[t][c] = 0.0f;
 }
 
+// Item state of one consumer warp (each warp follows the item sequence on its own).
+struct WarpItem {
+    Geo g;
+    RunInfo ri;
+    int slot[RUN_ROWS];
+};
+
+// Epilogue operands prefetched at item start by the warp that runs the epilogue of row `warp`:
+// type 1: svh_gate, svh_up, suh_down of the chunk; type 2: svh_down (fp16 x 4 per lane).
+struct EpiOps {
+    uint2 v[3][32];
+};
+
+template <int KR, int KS>
 __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -235,7 +283,8 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
     uint64_t* full = reinterpret_cast<uint64_t*>(res + RES_FLOATS);
     uint64_t* empty = full + NSTAGE;
     int* hdr = reinterpret_cast<int*>(empty + NSTAGE);   // [NSTAGE][2] item, stage
-    __shared__ int sh_slot[RUN_ROWS];
+    __shared__ WarpItem wis[NCW];
+    __shared__ EpiOps eps[RUN_ROWS];
     __shared__ int sh_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -291,8 +340,9 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                     mbar_arrive_expect_tx(&full[slot], nvalid * row_bytes);
                 }
                 __syncwarp();
-                if (lane < nvalid) bulk_g2s(ring + slot * (STAGE_BYTES / 4) + lane * (row_bytes / 4),
-                                            src + lane * row_stride, row_bytes, &full[slot]);
+                if (lane < nvalid)
+                    bulk_g2s(ring + slot * (STAGE_BYTES / 4) + lane * (row_bytes / 4), src + lane * row_stride, row_bytes,
+                             &full[slot]);
             }
             if (item < 0) break;
         }
@@ -300,17 +350,27 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
     }
 
     // ---------------------------------------------------------------------- consumers
-    float acc[NT][4];
+    float acc[WT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int t = 0; t < WT; ++t)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) acc[nt][c] = 0.0f;
+        for (int c = 0; c < 4; ++c) acc[t][c] = 0.0f;
 
+    const LaneGrp dR = lane_grp<KR>(lane);
+    const LaneGrp dS = lane_grp<KS>(lane);
+    const int quad = warp >> 1, whalf = warp & 1;
     const size_t S_tot = static_cast<size_t>(p.S_cap) + p.M;
+    const int nchH = p.H / 128;
+    WarpItem& wi = wis[warp];
     uint32_t q = 0;
+    uint32_t bc[2 * WR], bn[2 * WR];   // B of this warp's WR rows: current stage / next stage
+#pragma unroll
+    for (int i = 0; i < 2 * WR; ++i) bc[i] = bn[i] = 0;
+    float tsp[2] = {0.0f, 0.0f};       // epilogue warps: per-lane partial input sums (gate/up or down)
     int cur_item = -2;
-    Geo g;
-    RunInfo ri;
+    int sp = 0, proj = 0;              // stage within the projection, projection (0 gate / 1 up)
+    const __half* brow = nullptr;      // this lane's token row of the B input (projection 0)
+    size_t bproj = 0;                  // element offset from the gate to the up input
     for (;; ++q) {
         const int slot = q % NSTAGE;
         const uint32_t ph = (q / NSTAGE) & 1;
@@ -319,24 +379,67 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
         const int s = hdr[slot * 2 + 1];
         if (item < 0) break;
         if (item != cur_item) {
+            // item start, per warp: geometry, the run's slots, the dependency, epilogue prefetch
             cur_item = item;
-            g = item_geo(p, item);
-            ri = run_info(p, g.run);
-            if (tid < RUN_ROWS) sh_slot[tid] = tid < ri.nrows ? run_slot(p, g.run, tid) : 0;
-            if (tid == 0) {
-                if (g.type == 1) wait_geq(&p.ctr0[g.run], 1, p.status);
-                if (g.type == 2) wait_geq(&p.ctrA[g.run], ri.I / 128, p.status);
+            if (lane == 0) {
+                wi.g = item_geo(p, item);
+                wi.ri = run_info(p, wi.g.run);
             }
-            named_sync(1, NCW * 32);
+            __syncwarp();
+            const Geo g = wi.g;
+            const RunInfo ri = wi.ri;
+            if (lane < RUN_ROWS) wi.slot[lane] = lane < ri.nrows ? run_slot(p, g.run, lane) : run_slot(p, g.run, 0);
+            sp = 0;
+            proj = 0;
+            __syncwarp();
+            {
+                const int bs = wi.slot[lane >> 2];   // this lane's token row (rows past the run repeat row 0)
+                if (g.type == 1) {
+                    brow = p.xrot + static_cast<size_t>(bs) * p.hpad;
+                    bproj = S_tot * p.hpad;
+                } else {
+                    brow = p.act + static_cast<size_t>(bs) * p.ipad;
+                    bproj = 0;
+                }
+            }
+            if (lane == 0) {
+                if (g.type == 1) wait_geq(&p.ctr0[g.run], 1, p.status);
+                if (g.type == 2) wait_geq(&p.ctrA[g.run], (ri.I / 128) * ri.nrows, p.status);
+            }
+            __syncwarp();
+            if (g.type != 0 && warp < ri.nrows) {
+                const int sl = wi.slot[warp];
+                const int col = g.chunk * 128 + lane * 4;
+                if (g.type == 1) {
+                    cp_async8(&eps[warp].v[0][lane], static_cast<const __half*>(tensor_ptr(p, ri, 2)) + col);
+                    cp_async8(&eps[warp].v[1][lane], static_cast<const __half*>(tensor_ptr(p, ri, 5)) + col);
+                    cp_async8(&eps[warp].v[2][lane], static_cast<const __half*>(tensor_ptr(p, ri, 7)) + col);
+                    const float* xs0 = p.xsum + static_cast<size_t>(sl) * nchH;
+                    const float* xs1 = p.xsum + (S_tot + sl) * nchH;
+                    tsp[0] = tsp[1] = 0.0f;
+                    for (int c = g.kb / 8 + lane; c < g.ke / 8; c += 32) {
+                        tsp[0] += __ldcg(xs0 + c);
+                        tsp[1] += __ldcg(xs1 + c);
+                    }
+                } else {
+                    cp_async8(&eps[warp].v[0][lane], static_cast<const __half*>(tensor_ptr(p, ri, 8)) + col);
+                    const float* as = p.asum + static_cast<size_t>(sl) * (p.imax / 128);
+                    tsp[0] = 0.0f;
+                    for (int c = lane; c < ri.I / 128; c += 32) tsp[0] += __ldcg(as + c);
+                }
+                cp_async_commit();
+            }
         }
+        const int type = wi.g.type;
 
-        if (g.type == 0) {
-            // rotation of the run's rows for gate (suh row 1) and up (suh row 4)
+        if (type == 0) {
+            // rotation of the run's rows for gate (suh row 1) and up (suh row 4); CTA-wide
+            const RunInfo ri = wi.ri;
             const int nch = p.H / 128;
             const int units = ri.nrows * 2 * nch;
             for (int u = warp; u < units; u += NCW) {
                 const int t = u / (2 * nch), rem = u % (2 * nch), pj = rem / nch, c = rem % nch;
-                const int sl = sh_slot[t];
+                const int sl = wi.slot[t];
                 const int tok = slot_token(p, sl);
                 const int col = c * 128 + lane * 4;
                 float v[4], su[4];
@@ -345,47 +448,82 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) v[i] *= su[i];
                 had128_warp(v, lane);
-                store4_half(p.xrot + (static_cast<size_t>(pj) * S_tot + sl) * p.H + col, v);
+                store4_frag(p.xrot + (static_cast<size_t>(pj) * S_tot + sl) * p.hpad, col, v);
+                float sm = 0.0f;   // sum of the values as stored (fp16)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sm += __half2float(__float2half_rn(v[i]));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                if (lane == 0) p.xsum[(static_cast<size_t>(pj) * S_tot + sl) * nchH + c] = sm;
             }
             __threadfence();
             if (lane == 0) mbar_arrive(&empty[slot]);
             named_sync(1, NCW * 32);
-            if (tid == 0) atomicAdd(&p.ctr0[g.run], 1);
+            if (tid == 0) atomicAdd(&p.ctr0[wi.g.run], 1);
             continue;
         }
 
-        // GEMV stage
-        const int proj = g.type == 2 ? 0 : s / g.nsp;
-        const int kt0 = g.kb + (s % g.nsp) * STAGE_KT;
-        const int nvalid = min(STAGE_KT, g.ke - kt0);
-        const __half* src;
-        int width;
-        if (g.type == 1) {
-            src = p.xrot + static_cast<size_t>(proj) * S_tot * p.H;
-            width = p.H;
+        // GEMV stage: rows 4 quad .. 4 quad + 3 of the stage, B fragments prefetched one stage ahead
+        const int nsp = wi.g.nsp, kb = wi.g.kb, ke = wi.g.ke, nstages = wi.g.nstages;
+        const bool shared_run = wi.ri.shared;
+        const int kt0 = kb + sp * STAGE_KT;
+        const int r0 = kt0 + WR * quad;
+        if (s == 0) {
+            load_b4(brow, (kt0 >> 2) + quad, lane, bc);
         } else {
-            src = p.act;
-            width = p.imax;
+#pragma unroll
+            for (int i = 0; i < 2 * WR; ++i) bc[i] = bn[i];
         }
-        const uint32_t* buf = ring + slot * (STAGE_BYTES / 4);
-        switch (ri.K) {
-            case 2: gemv_stage<2>(buf, nvalid, warp, lane, src, width, kt0, sh_slot, ri.nrows, acc); break;
-            case 3: gemv_stage<3>(buf, nvalid, warp, lane, src, width, kt0, sh_slot, ri.nrows, acc); break;
-            default: gemv_stage<4>(buf, nvalid, warp, lane, src, width, kt0, sh_slot, ri.nrows, acc); break;
+        const int sp1 = sp + 1 == nsp ? 0 : sp + 1;
+        const int proj1 = sp + 1 == nsp ? proj + 1 : proj;
+        if (s + 1 < nstages) load_b4(brow + proj1 * bproj, ((kb + sp1 * STAGE_KT) >> 2) + quad, lane, bn);
+        {
+            const uint32_t* buf = ring + slot * (STAGE_BYTES / 4);
+            if (!shared_run || KR == KS) {
+                const uint32_t* rowp = buf + ((WR * quad) * NT + WT * whalf) * 8 * KR;
+#pragma unroll
+                for (int r = 0; r < WR; ++r)
+                    if (r0 + r < ke) gemv_row<KR>(rowp + r * NT * 8 * KR, dR, bc[2 * r], bc[2 * r + 1], acc);
+            } else {
+                const uint32_t* rowp = buf + ((WR * quad) * NT + WT * whalf) * 8 * KS;
+#pragma unroll
+                for (int r = 0; r < WR; ++r)
+                    if (r0 + r < ke) gemv_row<KS>(rowp + r * NT * 8 * KS, dS, bc[2 * r], bc[2 * r + 1], acc);
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
 
-        const bool proj_end = (s % g.nsp) == g.nsp - 1;
+        const bool proj_end = sp + 1 == nsp;
+        const int cproj = proj;
+        sp = sp1;
+        proj = proj1;
         if (!proj_end) continue;
-        reduce_acc(acc, red, res + proj * RUN_ROWS * 128, tid, warp, lane);
-        if (s != g.nstages - 1) continue;
+        reduce_acc(acc, red, res + cproj * RUN_ROWS * 128, tid, warp, lane);
+        if (s != nstages - 1) continue;
 
         // ------------------------------------------------------------- item epilogues
-        if (g.type == 1) {
-            const int chA = ri.I / 128;
+        const Geo g = wi.g;
+        const RunInfo ri = wi.ri;
+        if (type == 1) {
             if (p.split_a > 1) {
-                // publish this split's partial sums; the last split of (run, chunk) finishes
+                // publish this split's partial sums (input-sum correction included); the last
+                // split of (run, chunk) finishes. CTA-wide.
+                if (warp < ri.nrows) {
+                    float t0 = tsp[0], t1 = tsp[1];
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+                        t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        res[warp * 128 + lane * 4 + i] += CB_C1 * t0;
+                        res[RUN_ROWS * 128 + warp * 128 + lane * 4 + i] += CB_C1 * t1;
+                    }
+                    tsp[0] = tsp[1] = 0.0f;
+                }
+                named_sync(1, NCW * 32);
                 const int pidx = (g.run * (p.imax / 128) + g.chunk) * p.split_a + g.ks;
                 float* dst = p.partA + static_cast<size_t>(pidx) * RES_FLOATS;
                 for (int i = tid; i < RES_FLOATS; i += NCW * 32) dst[i] = res[i];
@@ -396,7 +534,12 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                     sh_flag = old == p.split_a - 1;
                 }
                 named_sync(1, NCW * 32);
-                if (!sh_flag) continue;
+                const int last = sh_flag;
+                named_sync(1, NCW * 32);
+                if (!last) {
+                    if (warp < ri.nrows) cp_async_wait_all();
+                    continue;
+                }
                 __threadfence();
                 const float* base = p.partA + static_cast<size_t>((g.run * (p.imax / 128) + g.chunk) * p.split_a) * RES_FLOATS;
                 for (int i = tid; i < RES_FLOATS; i += NCW * 32) {
@@ -407,94 +550,123 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                 named_sync(1, NCW * 32);
             }
             if (warp < ri.nrows) {
-                const int t = warp, sl = sh_slot[t];
+                // this warp's row: output rotation, scales, activation, down-input rotation
+                const int t = warp, sl = wi.slot[t];
                 const int col = g.chunk * 128 + lane * 4;
+                float t0 = tsp[0], t1 = tsp[1];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+                    t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+                }
                 float gv[4], uv[4], sv[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    gv[i] = res[t * 128 + lane * 4 + i];
-                    uv[i] = res[RUN_ROWS * 128 + t * 128 + lane * 4 + i];
+                    gv[i] = res[t * 128 + lane * 4 + i] + CB_C1 * t0;
+                    uv[i] = res[RUN_ROWS * 128 + t * 128 + lane * 4 + i] + CB_C1 * t1;
                 }
+                cp_async_wait_all();
+                __syncwarp();
                 had128_warp(gv, lane);
                 had128_warp(uv, lane);
-                load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 2)) + col, sv);
+                load4_half(reinterpret_cast<const __half*>(&eps[t].v[0][lane]), sv);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) gv[i] *= sv[i];
-                load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 5)) + col, sv);
+                load4_half(reinterpret_cast<const __half*>(&eps[t].v[1][lane]), sv);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) uv[i] *= sv[i];
                 const int mode = ri.shared ? p.act_shared : p.act_routed;
                 float av[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) av[i] = act_gated(gv[i], uv[i], p.limit, mode);
-                load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 7)) + col, sv);
+                load4_half(reinterpret_cast<const __half*>(&eps[t].v[2][lane]), sv);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) av[i] *= sv[i];
                 had128_warp(av, lane);
-                store4_half(p.act + static_cast<size_t>(sl) * p.imax + col, av);
-                __threadfence();
-            }
-            named_sync(1, NCW * 32);
-            if (tid == 0) atomicAdd(&p.ctrA[g.run], 1);
-            (void) chA;
-        } else {
-            // down epilogue: rotate, scale, weight; last arrival of (token, chunk) combines
-            if (warp < ri.nrows) {
-                const int t = warp, sl = sh_slot[t];
-                const int tok = slot_token(p, sl);
-                const int col = g.chunk * 128 + lane * 4;
-                float v[4], sv[4];
+                store4_frag(p.act + static_cast<size_t>(sl) * p.ipad, col, av);
+                float sm = 0.0f;   // sum of the values as stored (fp16)
 #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] = res[t * 128 + lane * 4 + i];
-                had128_warp(v, lane);
-                load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 8)) + col, sv);
-                const float wgt = ri.shared ? 1.0f : p.rw[sl];
+                for (int i = 0; i < 4; ++i) sm += __half2float(__float2half_rn(av[i]));
 #pragma unroll
-                for (int i = 0; i < 4; ++i) v[i] = v[i] * sv[i] * wgt;
-                *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(sl) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
+                for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                if (lane == 0) p.asum[static_cast<size_t>(sl) * (p.imax / 128) + g.chunk] = sm;
                 __threadfence();
                 __syncwarp();
-                int last = 0;
-                if (lane == 0) {
-                    const int old = atomicAdd(&p.ctrB[tok * (p.H / 128) + g.chunk], 1);
-                    last = old == p.tok_expect[tok] - 1;
+                if (lane == 0) atomicAdd(&p.ctrA[g.run], 1);
+            }
+        } else if (warp < ri.nrows) {
+            // down epilogue of this warp's row: rotate, scale, weight; the last arrival of
+            // (token, chunk) combines the token's slots in slot order, then the shared expert
+            const int t = warp, sl = wi.slot[t];
+            const int tok = slot_token(p, sl);
+            const int col = g.chunk * 128 + lane * 4;
+            float t0 = tsp[0];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+            float v[4], sv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = res[t * 128 + lane * 4 + i] + CB_C1 * t0;
+            cp_async_wait_all();
+            __syncwarp();
+            had128_warp(v, lane);
+            load4_half(reinterpret_cast<const __half*>(&eps[t].v[0][lane]), sv);
+            const float wgt = ri.shared ? 1.0f : p.rw[sl];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) v[i] = v[i] * sv[i] * wgt;
+            *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(sl) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
+            __threadfence();
+            __syncwarp();
+            int last = 0;
+            if (lane == 0) {
+                const int old = atomicAdd(&p.ctrB[tok * (p.H / 128) + g.chunk], 1);
+                last = old == p.tok_expect[tok] - 1;
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            if (last) {
+                __threadfence();
+                float o[4] = {0.f, 0.f, 0.f, 0.f};
+                for (int k = 0; k < p.topk; ++k) {
+                    const int s2 = tok * p.topk + k;
+                    if (!p.slot_act[s2]) continue;
+                    const float4 d = __ldcg(reinterpret_cast<const float4*>(p.dpart + static_cast<size_t>(s2) * p.H + col));
+                    o[0] += d.x;
+                    o[1] += d.y;
+                    o[2] += d.z;
+                    o[3] += d.w;
                 }
-                last = __shfl_sync(0xffffffffu, last, 0);
-                if (last) {
-                    __threadfence();
-                    float o[4] = {0.f, 0.f, 0.f, 0.f};
-                    for (int k = 0; k < p.topk; ++k) {
-                        const int s2 = tok * p.topk + k;
-                        if (!p.slot_act[s2]) continue;
-                        const float4 d = __ldcg(reinterpret_cast<const float4*>(p.dpart + static_cast<size_t>(s2) * p.H + col));
-                        o[0] += d.x;
-                        o[1] += d.y;
-                        o[2] += d.z;
-                        o[3] += d.w;
-                    }
-                    if (p.has_shared) {
-                        const float4 d = __ldcg(reinterpret_cast<const float4*>(
-                            p.dpart + (static_cast<size_t>(p.S_cap) + tok) * p.H + col));
-                        o[0] += d.x;
-                        o[1] += d.y;
-                        o[2] += d.z;
-                        o[3] += d.w;
-                    }
-                    const size_t oi = static_cast<size_t>(tok) * p.H + col;
-                    if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + oi) = make_float4(o[0], o[1], o[2], o[3]);
-                    if (p.out_bf16) {
-                        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]);
-                        __nv_bfloat162 hi = __floats2bfloat162_rn(o[2], o[3]);
-                        uint2 u;
-                        u.x = *reinterpret_cast<uint32_t*>(&lo);
-                        u.y = *reinterpret_cast<uint32_t*>(&hi);
-                        *reinterpret_cast<uint2*>(p.out_bf16 + oi) = u;
-                    }
+                if (p.has_shared) {
+                    const float4 d = __ldcg(reinterpret_cast<const float4*>(
+                        p.dpart + (static_cast<size_t>(p.S_cap) + tok) * p.H + col));
+                    o[0] += d.x;
+                    o[1] += d.y;
+                    o[2] += d.z;
+                    o[3] += d.w;
+                }
+                const size_t oi = static_cast<size_t>(tok) * p.H + col;
+                if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + oi) = make_float4(o[0], o[1], o[2], o[3]);
+                if (p.out_bf16) {
+                    __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]);
+                    __nv_bfloat162 hi = __floats2bfloat162_rn(o[2], o[3]);
+                    uint2 u;
+                    u.x = *reinterpret_cast<uint32_t*>(&lo);
+                    u.y = *reinterpret_cast<uint32_t*>(&hi);
+                    *reinterpret_cast<uint2*>(p.out_bf16 + oi) = u;
                 }
             }
-            named_sync(1, NCW * 32);
         }
     }
+    cp_async_wait_all();
+}
+
+using ExpertsKernel = void (*)(KParams);
+
+static ExpertsKernel pick_kernel(int kr, int ks)
+{
+#define EVA_K(a, b) \
+    if (kr == a && ks == b) return experts_kernel<a, b>;
+    EVA_K(2, 2) EVA_K(2, 3) EVA_K(2, 4) EVA_K(3, 2) EVA_K(3, 3) EVA_K(3, 4) EVA_K(4, 2) EVA_K(4, 3) EVA_K(4, 4)
+#undef EVA_K
+    return nullptr;
 }
 
 cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
@@ -516,6 +688,8 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
     p.has_shared = s.shared_inter > 0;
     p.S_cap = a.M * s.topk;
     p.imax = L.imax;
+    p.hpad = L.hpad;
+    p.ipad = L.ipad;
     p.act_routed = s.act_routed;
     p.act_shared = s.act_shared;
     p.limit = s.swiglu_limit;
@@ -534,6 +708,8 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
     p.act = reinterpret_cast<__half*>(ws + L.act);
     p.dpart = reinterpret_cast<float*>(ws + L.dpart);
     p.partA = reinterpret_cast<float*>(ws + L.partA);
+    p.xsum = reinterpret_cast<float*>(ws + L.xsum);
+    p.asum = reinterpret_cast<float*>(ws + L.asum);
     p.ctr_work = ctr + C.work;
     p.ctr0 = ctr + C.ctr0;
     p.ctrA = ctr + C.ctrA;
@@ -548,19 +724,17 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
     const int r_max = a.M * s.topk + (p.has_shared ? (a.M + RUN_ROWS - 1) / RUN_ROWS : 0);
     const int items_a = r_max * (L.imax / 128);
     int split = 1;
-    while (split < L.max_split && items_a * split * 2 <= 2 * sms && items_a * split * 2 <= PARTA_ITEMS) split *= 2;
+    // a split boundary must fall on a 128 chunk of the input (per-chunk input sums)
+    while (split < L.max_split && items_a * split * 2 <= 2 * sms && items_a * split * 2 <= PARTA_ITEMS &&
+           (s.hidden / 128) % (split * 2) == 0)
+        split *= 2;
     p.split_a = split;
 
-    static int configured_device = -1;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured_device != dev) {
-        cudaError_t e = cudaFuncSetAttribute(experts_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(SMEM_BYTES));
-        if (e != cudaSuccess) return e;
-        configured_device = dev;
-    }
-    experts_kernel<<<sms, THREADS, SMEM_BYTES, stream>>>(p);
+    const ExpertsKernel kern = pick_kernel(p.K, p.K_sh);
+    if (!kern) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return e;
+    kern<<<sms, THREADS, SMEM_BYTES, stream>>>(p);
     return cudaGetLastError();
 }
 

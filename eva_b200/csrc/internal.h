@@ -17,8 +17,9 @@ constexpr int ROUTER_KSLICE = 512;   // k elements per router GEMV warp
 struct WsLayout {
     int max_rows, S, R, imax, nchA, nchH, ks_router;
     size_t status, counters, n_counters, runs, run_expert, estart, slot_act, tok_expect;
-    size_t logits, idx, w, xrot, act, dpart, partA, total;
+    size_t logits, idx, w, xrot, act, dpart, partA, xsum, asum, total;
     int max_split;   // largest gate/up k-split the partial buffer allows (1 = none)
+    int hpad, ipad;  // row widths (halves) of the fragment-layout input buffers (one stage of slack)
 };
 
 // allow_split = false leaves out the split-k partial buffer (gate/up items are then never split).
