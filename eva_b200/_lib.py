@@ -19,7 +19,7 @@ ACT_CLAMP_AFTER, ACT_CLAMP_BEFORE = 0, 1
 # every symbol include/eva_moe.h declares
 EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_status", "eva_moe_route",
            "eva_moe_topk", "eva_moe_permute", "eva_moe_experts", "eva_moe_forward", "eva_exl3_dequant",
-           "eva_moe_arch", "eva_moe_experts_noalloc")
+           "eva_moe_arch", "eva_moe_experts_noalloc", "eva_moe_experts_decode", "eva_moe_experts_prefill")
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
 
@@ -70,6 +70,10 @@ def load(build_if_missing: bool = True):
     L.eva_moe_permute.argtypes = [shp, vp, i32, vp, i32, i32, vp, vp, vp]
     L.eva_moe_experts.restype = ctypes.c_int
     L.eva_moe_experts.argtypes = [shp, vp, i32, i32, vp, i32, vp, P(vp), P(ctypes.c_int64), vp, sz, vp, vp, vp]
+    for name in ("eva_moe_experts_decode", "eva_moe_experts_prefill"):
+        fn = getattr(L, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = [shp, vp, i32, i32, vp, i32, vp, P(vp), P(ctypes.c_int64), vp, sz, vp, vp, vp]
     L.eva_moe_forward.restype = ctypes.c_int
     L.eva_moe_forward.argtypes = [shp, vp, i32, i32, vp, vp, P(vp), P(ctypes.c_int64), vp, sz, vp, vp,
                                   vp, vp, vp, vp]

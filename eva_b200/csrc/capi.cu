@@ -50,6 +50,10 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split)
     L.dpart = take(St * H * 4);
     L.xsum = take(2 * St * L.nchH * 4);
     L.asum = take(St * L.nchA * 4);
+    L.tstart = take((E + 2) * 4);
+    L.pxg = take(St * H * 2);
+    L.pxu = take(St * H * 2);
+    L.pap = take(St * L.imax * 2);
     const size_t pa = allow_split ? std::min<size_t>(PARTA_ITEMS, R * L.nchA * 4) : 0;
     L.partA = take(pa * 2 * RUN_ROWS * 128 * 4);
     L.max_split = allow_split ? 4 : 1;
@@ -191,7 +195,7 @@ namespace eva {
 int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
                  int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
                  void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,
-                 bool allow_split)
+                 bool allow_split, int path)
 {
     if (!shape_ok(shape) || M < 0 || !x || !sel || !rw || !tables || !workspace) return EVA_ERR_INVALID;
     if (!out_f32 && !out_bf16) return EVA_ERR_INVALID;
@@ -212,6 +216,7 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
     pa.runs = reinterpret_cast<int32_t*>(ws + L.runs);
     pa.run_expert = reinterpret_cast<int32_t*>(ws + L.run_expert);
     pa.estart = reinterpret_cast<int32_t*>(ws + L.estart);
+    pa.tstart = reinterpret_cast<int32_t*>(ws + L.tstart);
     pa.slot_act = reinterpret_cast<int32_t*>(ws + L.slot_act);
     pa.tok_expect = reinterpret_cast<int32_t*>(ws + L.tok_expect);
     pa.counters = reinterpret_cast<int32_t*>(ws + L.counters);
@@ -238,7 +243,8 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
     ea.L = L;
     ea.out_f32 = out_f32;
     ea.out_bf16 = out_bf16;
-    return cuda_status(launch_experts(ea, st));
+    const bool tensor = path == 2 || (path == 0 && M >= PREFILL_MIN_ROWS);
+    return cuda_status(tensor ? launch_prefill(ea, st) : launch_experts(ea, st));
 }
 
 }  // namespace eva
@@ -251,6 +257,22 @@ int eva_moe_experts(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, 
 {
     return experts_impl(shape, x, x_is_bf16, M, sel, sel_is_i64, rw, tables, shared, workspace, workspace_bytes,
                         out_f32, out_bf16, static_cast<cudaStream_t>(stream));
+}
+
+int eva_moe_experts_prefill(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
+                            int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
+                            void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream)
+{
+    return experts_impl(shape, x, x_is_bf16, M, sel, sel_is_i64, rw, tables, shared, workspace, workspace_bytes,
+                        out_f32, out_bf16, static_cast<cudaStream_t>(stream), true, 2);
+}
+
+int eva_moe_experts_decode(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
+                           int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
+                           void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream)
+{
+    return experts_impl(shape, x, x_is_bf16, M, sel, sel_is_i64, rw, tables, shared, workspace, workspace_bytes,
+                        out_f32, out_bf16, static_cast<cudaStream_t>(stream), true, 1);
 }
 
 int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const float* router_w,

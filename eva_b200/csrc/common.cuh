@@ -64,13 +64,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
-// Bounded wait on an mbarrier phase. Returns false (and flags ST_TIMEOUT) when it gives up.
+__device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
+
+// Bounded wait on an mbarrier phase. Returns false (and flags ST_TIMEOUT) when it gives up. Once
+// any wait of the launch has given up, later waits return at once, so a systematic failure costs
+// one wait limit, not one per stage.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status)
 {
     if (mbar_try_wait(bar, parity)) return true;
+    if (ld_volatile(status) & ST_TIMEOUT) return false;
     const uint64_t t0 = globaltimer();
     while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+        if (globaltimer() - t0 > WAIT_LIMIT_NS || (ld_volatile(status) & ST_TIMEOUT)) {
             atomicOr(status, ST_TIMEOUT);
             return false;
         }
@@ -101,10 +106,11 @@ __device__ __forceinline__ int ld_acquire(const int* p)
 __device__ __forceinline__ bool wait_geq(const int* p, int target, int* status)
 {
     if (ld_acquire(p) >= target) return true;
+    if (ld_volatile(status) & ST_TIMEOUT) return false;
     const uint64_t t0 = globaltimer();
     while (ld_acquire(p) < target) {
         __nanosleep(64);
-        if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+        if (globaltimer() - t0 > WAIT_LIMIT_NS || (ld_volatile(status) & ST_TIMEOUT)) {
             atomicOr(status, ST_TIMEOUT);
             return false;
         }

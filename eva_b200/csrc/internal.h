@@ -18,6 +18,7 @@ struct WsLayout {
     int max_rows, S, R, imax, nchA, nchH, ks_router;
     size_t status, counters, n_counters, runs, run_expert, estart, slot_act, tok_expect;
     size_t logits, idx, w, xrot, act, dpart, partA, xsum, asum, total;
+    size_t tstart, pxg, pxu, pap;   // prefill: tile prefix, sorted rotated inputs, sorted down inputs
     int max_split;   // largest gate/up k-split the partial buffer allows (1 = none)
     int hpad, ipad;  // row widths (halves) of the fragment-layout input buffers (one stage of slack)
 };
@@ -45,6 +46,7 @@ struct PermuteArgs {
     int32_t* runs;
     int32_t* run_expert;        // may be null
     int32_t* estart;            // may be null
+    int32_t* tstart;            // may be null: [E + 2] prefix of 128-row tiles per expert (+ shared)
     int32_t* slot_act;          // may be null
     int32_t* tok_expect;        // may be null
     int32_t* counters;          // zeroed when non-null
@@ -70,12 +72,15 @@ struct ExpertsArgs {
     void* out_bf16;
 };
 cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream);
+cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream);
+
+constexpr int PREFILL_MIN_ROWS = 129;   // eva_moe_experts takes the tensor-core path from this many rows
 
 // Permutation + fused experts on a caller-provided workspace laid out by ws_layout(shape, M, allow_split).
 int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
                  int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
                  void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,
-                 bool allow_split = true);
+                 bool allow_split = true, int path = 0);   // path: 0 by size, 1 decode kernel, 2 tensor-core
 
 cudaError_t launch_dequant(const void* trellis, int in, int out, int K, uint16_t* w, cudaStream_t stream);
 

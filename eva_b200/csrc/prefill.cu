@@ -1,0 +1,634 @@
+// Prefill-shaped MoE experts on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// Tokens are grouped by expert (the permutation's sorted order), so each expert is a dense
+// [rows x H] x [H x I] problem. Per CTA one 128-row x 128-column output tile:
+//   warp 0      producer: 2-D TMA loads (128B swizzle, no multicast) of the rotated input rows
+//               and 1-D bulk copies of the EXL3 trellis rows of the k-block into a 5-stage ring
+//   warps 2-9   decoders: EXL3 decode of the k-block's 32 weight tiles (exact fp16, one rounding)
+//               straight into the UMMA K-major 128B-swizzled shared-memory layout
+//   warp 1      one thread issues tcgen05.mma (M=128, N=128, K=16, fp16 x fp16 -> fp32 in TMEM)
+//               and commits each stage back to the producer through an mbarrier
+//   all warps   epilogue: tcgen05.ld of the accumulators, Hadamard / scales / activation in
+//               registers, fp16 or fp32 stores.
+// Kernels:
+//   pf_rotate    x -> fp16(H128(x * suh)) for gate and up, rows in expert-sorted order
+//   pf_gateup    gate and up accumulators (TMEM columns 0-127 / 128-255), epilogue = the MoE
+//                coop A epilogue (exl3_moe_coop_kernel.cuh:758-808): H128, svh, SiLU*mul, suh_down,
+//                H128 -> fp16 down input
+//   pf_down      down projection, epilogue H128 * svh * routing weight -> per-slot fp32 rows
+//   pf_combine   per token: slots in slot order, then the shared expert (as the coop B kernel,
+//                exl3_moe_coop_kernel.cuh:906-949) -> bf16 / fp32 output
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace eva {
+
+constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;
+constexpr int PF_STAGES = 5;
+constexpr int PF_DEC = 8;                                // decoder warps
+constexpr int NT_PF = 8;                                 // 16-column tiles per 128-column chunk
+constexpr int PF_THREADS = (2 + PF_DEC) * 32;
+constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB
+constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;            // 16 KB
+constexpr int PF_T_BYTES = 4 * 8 * 32 * 4;               // 4 k-tile rows x 8 tiles x 32K bytes (K <= 4)
+constexpr int PF_STAGE = PF_A_BYTES + PF_B_BYTES + PF_T_BYTES;
+constexpr int PF_EPI_LD = 129;                           // padded row (floats) of the epilogue tiles
+constexpr size_t PF_SMEM = 1024 + static_cast<size_t>(PF_STAGES) * PF_STAGE + 256;
+static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PF_STAGES * PF_STAGE, "epilogue tiles reuse the ring");
+
+struct PfParams {
+    int M, H, I, I_sh, topk, S_cap, n_local, K, K_sh, has_shared, imax, act_routed, act_shared;
+    float limit;
+    const void* x;
+    int x_bf16;
+    const float* rw;
+    const int64_t* tables[9];
+    int64_t sh[9];
+    const int* runs;        // reference-layout run table (order[] = slots in expert order)
+    const int* estart;      // [E + 1] first sorted row of each expert
+    const int* tstart;      // [E + 2] first 128-row tile of each expert; [E + 1] = total incl. shared
+    const void* sel;
+    int sel64;
+    __half* xg;             // [S_cap + M][H] rotated gate inputs, sorted rows (shared rows at S_cap)
+    __half* xu;             // [S_cap + M][H] rotated up inputs
+    __half* ap;             // [S_cap + M][imax] down inputs
+    float* dpart;           // [S_cap + M][H] per-slot weighted down outputs
+    const int* slot_act;
+    float* out_f32;
+    __nv_bfloat16* out_bf16;
+    int* status;
+};
+
+// ---------------------------------------------------------------------------------------------
+// tcgen05 / TMA helpers
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr)
+{
+    // K-major, 128B swizzle: 8-row core groups 1024 B apart (SBO), LBO unused (1), version 1
+    return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+
+// kind::f16 instruction descriptor: fp16 A and B (K-major), fp32 accumulator, M x N
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N)
+{
+    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of element (row, k) (k < 64, fp16) in a K-major 128B-swizzled 128 x 64 tile.
+__device__ __forceinline__ uint32_t sw128_off(int row, int k)
+{
+    const int kb = k * 2;
+    return row * 128 + ((((kb >> 4) ^ (row & 7)) << 4) | (kb & 15));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Tile -> expert. Experts 0..E-1 routed, E = shared.
+
+struct PfTile {
+    int e;         // expert, n_local = shared
+    int row0;      // first sorted row of the tile
+    int rows;      // valid rows (<= 128)
+    bool shared;
+};
+
+__device__ __forceinline__ bool pf_tile(const PfParams& p, int mt, PfTile& t)
+{
+    const int E = p.n_local;
+    if (mt >= p.tstart[E + 1]) return false;
+    if (mt >= p.tstart[E]) {
+        t.e = E;
+        t.shared = true;
+        const int j = mt - p.tstart[E];
+        t.row0 = p.S_cap + j * PF_BM;
+        t.rows = min(PF_BM, p.M - j * PF_BM);
+        return true;
+    }
+    int lo = 0, hi = E - 1;   // last e with tstart[e] <= mt
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (p.tstart[mid] <= mt) lo = mid;
+        else hi = mid - 1;
+    }
+    t.e = lo;
+    t.shared = false;
+    const int j = mt - p.tstart[lo];
+    t.row0 = p.estart[lo] + j * PF_BM;
+    t.rows = min(PF_BM, p.estart[lo + 1] - t.row0);
+    return true;
+}
+
+__device__ __forceinline__ int64_t pf_ptr(const PfParams& p, const PfTile& t, int row)
+{
+    return t.shared ? p.sh[row] : p.tables[row][t.e];
+}
+
+__device__ __forceinline__ int pf_row_slot(const PfParams& p, int pos)
+{
+    return pos >= p.S_cap ? pos : p.runs[2 + p.S_cap + 1 + pos];
+}
+
+// ---------------------------------------------------------------------------------------------
+// pf_rotate: warp per (sorted row, 128 chunk, projection)
+
+__global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = p.H / 128;
+    const long long item = static_cast<long long>(blockIdx.x) * 8 + warp;
+    const long long rows = static_cast<long long>(p.S_cap) + p.M;
+    if (item >= rows * nch * 2) return;
+    const int pos = static_cast<int>(item / (nch * 2));
+    const int rem = static_cast<int>(item % (nch * 2));
+    const int c = rem >> 1, pj = rem & 1;
+    int tok;
+    const __half* suh;
+    if (pos >= p.S_cap) {
+        if (!p.has_shared) return;
+        tok = pos - p.S_cap;
+        suh = reinterpret_cast<const __half*>(p.sh[pj ? 4 : 1]);
+    } else {
+        if (pos >= p.runs[2 + p.runs[0]]) return;   // past the active rows
+        const int slot = p.runs[2 + p.S_cap + 1 + pos];
+        tok = slot / p.topk;
+        const long long e = p.sel64 ? static_cast<const long long*>(p.sel)[slot] : static_cast<const int*>(p.sel)[slot];
+        suh = reinterpret_cast<const __half*>(p.tables[pj ? 4 : 1][e]);
+    }
+    const int col = c * 128 + lane * 4;
+    float v[4], su[4];
+    load4_x(p.x, static_cast<size_t>(tok) * p.H + col, p.x_bf16, v);
+    load4_half_ro(suh + col, su);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] *= su[i];
+    had128_warp(v, lane);
+    store4_half((pj ? p.xu : p.xg) + static_cast<size_t>(pos) * p.H + col, v);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Shared main loop of the two GEMM kernels.
+//   nproj   projections accumulated (gate+up: 2, down: 1), each into its own 128 TMEM columns
+//   nkb     k-blocks (64) per projection
+//   amaps   tensor maps of the A rows per projection; trellis bases per projection
+
+struct PfLoop {
+    const CUtensorMap* amap[2];
+    const uint8_t* trellis[2];
+    size_t row_stride;       // bytes between k-tile rows of the trellis
+    int chunk;               // 128-column output chunk
+    int nproj, nkb, row0;
+};
+
+template <int K>
+__device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, uint64_t* full, uint64_t* dec, uint64_t* empty,
+                                            uint64_t* accb, uint32_t tmem, int warp, int lane, int* status)
+{
+    const int total = L.nproj * L.nkb;
+    constexpr uint32_t TROW = NT_PF * 32 * K;   // bytes of one k-tile row's 8 tiles
+    if (warp == 0) {
+        // producer
+        for (int s = 0; s < total; ++s) {
+            const int st = s % PF_STAGES;
+            const uint32_t ph = (s / PF_STAGES) & 1;
+            mbar_wait(&empty[st], ph ^ 1, status);
+            const int pj = s / L.nkb, kb = s % L.nkb;
+            uint8_t* stage = ring + st * PF_STAGE;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[st], PF_A_BYTES + 4 * TROW);
+                tma_load_2d(stage, L.amap[pj], kb * PF_BK, L.row0, &full[st]);
+            }
+            __syncwarp();
+            if (lane < 4)
+                bulk_g2s(stage + PF_A_BYTES + PF_B_BYTES + lane * TROW,
+                         L.trellis[pj] + static_cast<size_t>(kb * 4 + lane) * L.row_stride + static_cast<size_t>(L.chunk) * TROW,
+                         TROW, &full[st]);
+        }
+    } else if (warp == 1) {
+        // MMA issuer
+        constexpr uint32_t idesc = umma_idesc_f16(PF_BM, PF_BN);
+        for (int s = 0; s < total; ++s) {
+            const int st = s % PF_STAGES;
+            const uint32_t ph = (s / PF_STAGES) & 1;
+            mbar_wait(&full[st], ph, status);
+            mbar_wait(&dec[st], ph, status);
+            tc_fence_after();
+            const int pj = s / L.nkb, kb = s % L.nkb;
+            if (lane == 0) {
+                const uint32_t sa = smem_u32(ring + st * PF_STAGE);
+                const uint32_t sb = sa + PF_A_BYTES;
+#pragma unroll
+                for (int k = 0; k < PF_BK / 16; ++k)
+                    umma_f16(tmem + pj * PF_BN, umma_desc_sw128(sa + k * 32), umma_desc_sw128(sb + k * 32), idesc,
+                             (kb > 0 || k > 0) ? 1u : 0u);
+                umma_commit(&empty[st]);
+                if (s == total - 1) umma_commit(accb);
+            }
+            __syncwarp();
+        }
+    } else {
+        // decoders: warp d (0..7) takes k-tile row d / 2 of the block and tiles 4 (d % 2) .. +3
+        const int d = warp - 2;
+        const int ktl = d >> 1, nt0 = (d & 1) * 4;
+        const LaneDec ld = lane_dec<K>(lane);
+        const int n0 = lane >> 2, k0 = 2 * (lane & 3);
+        for (int s = 0; s < total; ++s) {
+            const int st = s % PF_STAGES;
+            const uint32_t ph = (s / PF_STAGES) & 1;
+            mbar_wait(&full[st], ph, status);
+            uint8_t* stage = ring + st * PF_STAGE;
+            const uint32_t* tr = reinterpret_cast<const uint32_t*>(stage + PF_A_BYTES + PF_B_BYTES + ktl * TROW);
+            uint8_t* bt = stage + PF_A_BYTES;
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                uint32_t a[4];
+                decode_afrag<K>(tr + (nt0 + t) * 8 * K, ld, a);
+                const int n = (nt0 + t) * 16 + n0;   // output column within the chunk (B row)
+                const int k = ktl * 16 + k0;          // k within the 64-wide block
+                *reinterpret_cast<uint32_t*>(bt + sw128_off(n, k)) = a[0];
+                *reinterpret_cast<uint32_t*>(bt + sw128_off(n, k + 8)) = a[2];
+                *reinterpret_cast<uint32_t*>(bt + sw128_off(n + 8, k)) = a[1];
+                *reinterpret_cast<uint32_t*>(bt + sw128_off(n + 8, k + 8)) = a[3];
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&dec[st]);
+        }
+    }
+}
+
+// TMEM accumulator (columns col0 .. col0 + 127) -> smem tile [128][PF_EPI_LD] by warps 0-3
+// (warp w reads TMEM lanes 32 w .. 32 w + 31).
+__device__ __forceinline__ void pf_tmem_to_smem(uint32_t tmem, int col0, float* tile, int warp, int lane)
+{
+    const int row = warp * 32 + lane;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + col0 + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) tile[row * PF_EPI_LD + c * 32 + i] = v[i];
+    }
+}
+
+struct PfSmem {
+    uint64_t full[PF_STAGES], dec[PF_STAGES], empty[PF_STAGES], accb;
+    uint32_t tmem;
+};
+
+__device__ __forceinline__ uint8_t* pf_ring(uint8_t* raw)
+{
+    const uint32_t a = smem_u32(raw);
+    return raw + ((1024 - (a & 1023)) & 1023);
+}
+
+__device__ __forceinline__ void pf_setup(PfSmem& S, int warp, int ncols)
+{
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PF_STAGES; ++i) {
+            mbar_init(&S.full[i], 1);
+            mbar_init(&S.dec[i], PF_DEC);
+            mbar_init(&S.empty[i], 1);
+        }
+        mbar_init(&S.accb, 1);
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem)), "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+}
+
+__device__ __forceinline__ void pf_teardown(PfSmem& S, int warp, int ncols)
+{
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(S.tmem), "r"(ncols));
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// pf_gateup: gate and up of one (expert tile, 128 columns of I)
+
+template <int KR, int KS>
+__global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, const __grid_constant__ CUtensorMap mg,
+                                                          const __grid_constant__ CUtensorMap mu)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ PfSmem S;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    PfTile t;
+    if (!pf_tile(p, blockIdx.x, t)) return;
+    const int I_e = t.shared ? p.I_sh : p.I;
+    const int chunk = blockIdx.y;
+    if (chunk * 128 >= I_e) return;
+    const int Ke = t.shared ? KS : KR;
+    uint8_t* ring = pf_ring(smem_raw);
+    pf_setup(S, warp, 256);
+
+    PfLoop L;
+    L.amap[0] = &mg;
+    L.amap[1] = &mu;
+    L.trellis[0] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 0));
+    L.trellis[1] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 3));
+    L.row_stride = static_cast<size_t>(I_e / 16) * 32 * Ke;
+    L.chunk = chunk;
+    L.nproj = 2;
+    L.nkb = p.H / PF_BK;
+    L.row0 = t.row0;
+    if (Ke == KR) pf_mainloop<KR>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
+    else pf_mainloop<KS>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
+
+    // epilogue
+    mbar_wait(&S.accb, 0, p.status);
+    tc_fence_after();
+    float* G = reinterpret_cast<float*>(ring);
+    float* U = G + PF_BM * PF_EPI_LD;
+    if (warp < 4) {
+        pf_tmem_to_smem(S.tmem, 0, G, warp, lane);
+        pf_tmem_to_smem(S.tmem, PF_BN, U, warp, lane);
+    }
+    __syncthreads();
+    const int col = chunk * 128 + lane * 4;
+    float svg[4], svu[4], sud[4];
+    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 2)) + col, svg);
+    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 5)) + col, svu);
+    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 7)) + col, sud);
+    const int mode = t.shared ? p.act_shared : p.act_routed;
+    for (int r = warp; r < t.rows; r += PF_THREADS / 32) {
+        float g[4], u[4], a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            g[i] = G[r * PF_EPI_LD + lane * 4 + i];
+            u[i] = U[r * PF_EPI_LD + lane * 4 + i];
+        }
+        had128_warp(g, lane);
+        had128_warp(u, lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a[i] = act_gated(g[i] * svg[i], u[i] * svu[i], p.limit, mode) * sud[i];
+        had128_warp(a, lane);
+        store4_half(p.ap + static_cast<size_t>(t.row0 + r) * p.imax + col, a);
+    }
+    pf_teardown(S, warp, 256);
+}
+
+// ---------------------------------------------------------------------------------------------
+// pf_down: down projection of one (expert tile, 128 columns of H), weighted per-slot rows
+
+template <int KR, int KS>
+__global__ void __launch_bounds__(PF_THREADS, 1) pf_down(const PfParams p, const __grid_constant__ CUtensorMap ma)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ PfSmem S;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    PfTile t;
+    if (!pf_tile(p, blockIdx.x, t)) return;
+    const int I_e = t.shared ? p.I_sh : p.I;
+    const int chunk = blockIdx.y;
+    const int Ke = t.shared ? KS : KR;
+    uint8_t* ring = pf_ring(smem_raw);
+    pf_setup(S, warp, 128);
+
+    PfLoop L;
+    L.amap[0] = L.amap[1] = &ma;
+    L.trellis[0] = L.trellis[1] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 6));
+    L.row_stride = static_cast<size_t>(p.H / 16) * 32 * Ke;
+    L.chunk = chunk;
+    L.nproj = 1;
+    L.nkb = I_e / PF_BK;
+    L.row0 = t.row0;
+    if (Ke == KR) pf_mainloop<KR>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
+    else pf_mainloop<KS>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
+
+    mbar_wait(&S.accb, 0, p.status);
+    tc_fence_after();
+    float* D = reinterpret_cast<float*>(ring);
+    if (warp < 4) pf_tmem_to_smem(S.tmem, 0, D, warp, lane);
+    __syncthreads();
+    const int col = chunk * 128 + lane * 4;
+    float svd[4];
+    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 8)) + col, svd);
+    for (int r = warp; r < t.rows; r += PF_THREADS / 32) {
+        const int slot = pf_row_slot(p, t.row0 + r);
+        const float w = t.shared ? 1.0f : p.rw[slot];
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = D[r * PF_EPI_LD + lane * 4 + i];
+        had128_warp(v, lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] *= svd[i] * w;
+        *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(slot) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    pf_teardown(S, warp, 128);
+}
+
+// ---------------------------------------------------------------------------------------------
+// pf_combine: warp per (token, 128 chunk)
+
+__global__ void __launch_bounds__(256) pf_combine(const PfParams p)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = p.H / 128;
+    const long long item = static_cast<long long>(blockIdx.x) * 8 + warp;
+    if (item >= static_cast<long long>(p.M) * nch) return;
+    const int tok = static_cast<int>(item / nch), c = static_cast<int>(item % nch);
+    const int col = c * 128 + lane * 4;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < p.topk; ++k) {
+        const int s = tok * p.topk + k;
+        if (!p.slot_act[s]) continue;
+        const float4 d = *reinterpret_cast<const float4*>(p.dpart + static_cast<size_t>(s) * p.H + col);
+        o[0] += d.x;
+        o[1] += d.y;
+        o[2] += d.z;
+        o[3] += d.w;
+    }
+    if (p.has_shared) {
+        const float4 d = *reinterpret_cast<const float4*>(p.dpart + (static_cast<size_t>(p.S_cap) + tok) * p.H + col);
+        o[0] += d.x;
+        o[1] += d.y;
+        o[2] += d.z;
+        o[3] += d.w;
+    }
+    const size_t oi = static_cast<size_t>(tok) * p.H + col;
+    if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + oi) = make_float4(o[0], o[1], o[2], o[3]);
+    if (p.out_bf16) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(o[2], o[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&lo);
+        u.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(p.out_bf16 + oi) = u;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    return fn;
+}
+
+// fp16 [rows][cols] row-major, box 64 x 128, 128B swizzle
+static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols)
+{
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {PF_BK, PF_BM};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+using GateUpKernel = void (*)(PfParams, CUtensorMap, CUtensorMap);
+using DownKernel = void (*)(PfParams, CUtensorMap);
+
+template <int A, int B>
+static void pick(int kr, int ks, GateUpKernel& g, DownKernel& d)
+{
+    if (kr == A && ks == B) {
+        g = pf_gateup<A, B>;
+        d = pf_down<A, B>;
+    }
+}
+
+cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
+{
+    const EvaMoeShape& s = *a.shape;
+    const WsLayout& L = a.L;
+    uint8_t* ws = static_cast<uint8_t*>(a.ws);
+    PfParams p{};
+    p.M = a.M;
+    p.H = s.hidden;
+    p.I = s.inter;
+    p.I_sh = s.shared_inter;
+    p.topk = s.topk;
+    p.S_cap = a.M * s.topk;
+    p.n_local = s.n_experts;
+    p.K = s.bits;
+    p.K_sh = s.shared_inter ? s.shared_bits : s.bits;
+    p.has_shared = s.shared_inter > 0;
+    p.imax = L.imax;
+    p.act_routed = s.act_routed;
+    p.act_shared = s.act_shared;
+    p.limit = s.swiglu_limit;
+    p.x = a.x;
+    p.x_bf16 = a.x_bf16;
+    p.rw = a.rw;
+    for (int i = 0; i < 9; ++i) {
+        p.tables[i] = a.tables[i];
+        p.sh[i] = a.shared[i];
+    }
+    p.runs = reinterpret_cast<const int*>(ws + L.runs);
+    p.estart = reinterpret_cast<const int*>(ws + L.estart);
+    p.tstart = reinterpret_cast<const int*>(ws + L.tstart);
+    p.sel = a.sel;
+    p.sel64 = a.sel64;
+    p.xg = reinterpret_cast<__half*>(ws + L.pxg);
+    p.xu = reinterpret_cast<__half*>(ws + L.pxu);
+    p.ap = reinterpret_cast<__half*>(ws + L.pap);
+    p.dpart = reinterpret_cast<float*>(ws + L.dpart);
+    p.slot_act = reinterpret_cast<const int*>(ws + L.slot_act);
+    p.out_f32 = a.out_f32;
+    p.out_bf16 = static_cast<__nv_bfloat16*>(a.out_bf16);
+    p.status = reinterpret_cast<int*>(ws + L.status);
+
+    const uint64_t rows = static_cast<uint64_t>(p.S_cap) + p.M;
+    CUtensorMap mg, mu, ma;
+    if (!make_map(&mg, p.xg, rows, p.H) || !make_map(&mu, p.xu, rows, p.H) || !make_map(&ma, p.ap, rows, p.imax))
+        return cudaErrorInvalidValue;
+
+    GateUpKernel kg = nullptr;
+    DownKernel kd = nullptr;
+    pick<2, 2>(p.K, p.K_sh, kg, kd);
+    pick<2, 3>(p.K, p.K_sh, kg, kd);
+    pick<2, 4>(p.K, p.K_sh, kg, kd);
+    pick<3, 2>(p.K, p.K_sh, kg, kd);
+    pick<3, 3>(p.K, p.K_sh, kg, kd);
+    pick<3, 4>(p.K, p.K_sh, kg, kd);
+    pick<4, 2>(p.K, p.K_sh, kg, kd);
+    pick<4, 3>(p.K, p.K_sh, kg, kd);
+    pick<4, 4>(p.K, p.K_sh, kg, kd);
+    if (!kg || !kd) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(kg, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(PF_SMEM));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(PF_SMEM));
+    if (e != cudaSuccess) return e;
+
+    const long long rot_items = static_cast<long long>(rows) * (p.H / 128) * 2;
+    pf_rotate<<<static_cast<unsigned>((rot_items + 7) / 8), 256, 0, stream>>>(p);
+    // tile upper bound: sum over experts of ceil(n_e / 128) <= S / 128 + E, plus the shared tiles
+    const int max_tiles = (p.S_cap + PF_BM - 1) / PF_BM + p.n_local + (p.has_shared ? (p.M + PF_BM - 1) / PF_BM : 0);
+    const int imax_ch = L.imax / 128;
+    kg<<<dim3(max_tiles, imax_ch), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
+    kd<<<dim3(max_tiles, p.H / 128), PF_THREADS, PF_SMEM, stream>>>(p, ma);
+    const long long comb = static_cast<long long>(p.M) * (p.H / 128);
+    pf_combine<<<static_cast<unsigned>((comb + 7) / 8), 256, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace eva

@@ -323,11 +323,13 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     int* hist = smem_i;              // [E]
     int* estart = hist + E;          // [E + 1]
     int* rstart = estart + E + 1;    // [E + 1]
-    int* cursor = rstart + E + 1;    // [E]
+    int* tsh = rstart + E + 1;       // [E + 1] tile prefix
+    int* cursor = tsh + E + 1;       // [E]
     int* wcnt = cursor + E;          // [32][E]
     __shared__ int sh_tot[2];
     __shared__ int scan_tmp[32];
     __shared__ int scan_tmp2[32];
+    __shared__ int scan_tmp3[32];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int S_cap = a.capacity * a.topk;
@@ -358,37 +360,45 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     {
         const int h = tid < E ? hist[tid] : 0;
         const int r = (h + RUN_ROWS - 1) / RUN_ROWS;
-        int v0 = h, v1 = r;
+        const int mt = (h + 127) / 128;
+        int v0 = h, v1 = r, v2 = mt;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const int n0 = __shfl_up_sync(0xffffffffu, v0, o);
             const int n1 = __shfl_up_sync(0xffffffffu, v1, o);
+            const int n2 = __shfl_up_sync(0xffffffffu, v2, o);
             if (lane >= o) {
                 v0 += n0;
                 v1 += n1;
+                v2 += n2;
             }
         }
         if (lane == 31) {
             scan_tmp[warp] = v0;
             scan_tmp2[warp] = v1;
+            scan_tmp3[warp] = v2;
         }
         __syncthreads();
-        int b0 = 0, b1 = 0, t0 = 0, t1 = 0;
+        int b0 = 0, b1 = 0, b2 = 0, t0 = 0, t1 = 0, t2 = 0;
         for (int w = 0; w < 32; ++w) {
             if (w < warp) {
                 b0 += scan_tmp[w];
                 b1 += scan_tmp2[w];
+                b2 += scan_tmp3[w];
             }
             t0 += scan_tmp[w];
             t1 += scan_tmp2[w];
+            t2 += scan_tmp3[w];
         }
         if (tid < E) {
             estart[tid] = b0 + v0 - h;
             rstart[tid] = b1 + v1 - r;
+            tsh[tid] = b2 + v2 - mt;
         }
         if (tid == 0) {
             estart[E] = t0;
             rstart[E] = t1;
+            tsh[E] = t2;
             sh_tot[0] = t0;   // active slots
             sh_tot[1] = t1;   // runs
         }
@@ -442,6 +452,10 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     }
     if (a.estart)
         for (int i = tid; i <= E; i += PERM_THREADS) a.estart[i] = estart[i];
+    if (a.tstart) {
+        for (int i = tid; i <= E; i += PERM_THREADS) a.tstart[i] = tsh[i];
+        if (tid == 0) a.tstart[E + 1] = tsh[E] + (a.has_shared ? (a.M + 127) / 128 : 0);
+    }
     __syncthreads();
 
     // 5. expected combine arrivals; rows nobody will write are zeroed here
@@ -464,7 +478,7 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
 
 cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t stream)
 {
-    const size_t smem = (static_cast<size_t>(a.n_local) * 4 + 2 + 32 * static_cast<size_t>(a.n_local)) * sizeof(int);
+    const size_t smem = (static_cast<size_t>(a.n_local) * 5 + 3 + 32 * static_cast<size_t>(a.n_local)) * sizeof(int);
     cudaError_t e = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     permute_kernel<<<1, PERM_THREADS, smem, stream>>>(a);

@@ -113,6 +113,19 @@ int eva_moe_experts(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, 
                     const int64_t* const* tables, const int64_t* shared,
                     void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream);
 
+/* eva_moe_experts forced onto one of its two implementations (eva_moe_experts picks by row count:
+ * the tensor-core path from 129 rows on). Same arguments and results.
+ *   _decode:  the persistent register-decode GEMV kernel (mma.sync), best for decode batches
+ *   _prefill: expert-sorted tcgen05 grouped GEMMs with TMEM accumulators (prefill) */
+int eva_moe_experts_decode(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
+                           const void* sel, int32_t sel_is_i64, const float* rw,
+                           const int64_t* const* tables, const int64_t* shared,
+                           void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream);
+int eva_moe_experts_prefill(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
+                            const void* sel, int32_t sel_is_i64, const float* rw,
+                            const int64_t* const* tables, const int64_t* shared,
+                            void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream);
+
 /* Whole layer: eva_moe_route + eva_moe_experts. idx_out / w_out / logits_out may be NULL. */
 int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
                     const float* router_w, const float* router_b,
