@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true", help="small case for ncu captures (64 experts)")
+    ap.add_argument("--prefill-tokens", type=int, default=4096)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--prefill-only", action="store_true")
     return ap.parse_args()
 
 
@@ -59,6 +62,91 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s for a kernel timed inside a long step (sustained figure)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("bf16_tflops_sustained", d.get("bf16_tflops"))), "measured (sustained)"
+    return 1400.0, "fallback (sustained)"
+
+
+ZIPF_S = 1.1
+ZIPF_BETA = 0.1
+
+
+def zipf_bias(cfg, base, seed=3):
+    """Router bias skewed toward a Zipf(1.1) expert load: beta * log(rank^-s), ranks permuted by seed."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(seed)
+    rank = np.empty(cfg.n_experts)
+    rank[rng.permutation(cfg.n_experts)] = np.arange(1, cfg.n_experts + 1)
+    off = torch.tensor(ZIPF_BETA * np.log(rank ** -ZIPF_S), dtype=torch.float32, device=base.device)
+    return (base + off).contiguous()
+
+
+def prefill_measure(cfg, layer, dev, steps, warmup, M):
+    """Prefill step (router + tensor-core experts) on M tokens with Zipf-skewed routing."""
+    import ctypes
+    import numpy as np
+    import torch
+    from eva_b200 import _lib
+    lib = _lib.load()
+    shape = _lib.shape_of(cfg)
+    ws = torch.empty(lib.eva_moe_workspace_bytes(ctypes.byref(shape), M), dtype=torch.uint8, device=dev)
+    ws.zero_()
+    bias = zipf_bias(cfg, layer.router_b)
+    tables = _lib.table_array(tuple(layer.packed.unbind(0)))
+    shared = _lib.shared_array(layer.shared.tolist()) if layer.shared is not None else None
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    xs = [torch.randn(M, cfg.hidden, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
+    idx = torch.empty(M, cfg.topk, dtype=torch.int32, device=dev)
+    w = torch.empty(M, cfg.topk, device=dev)
+    out = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+
+    def step(i, ev=None):
+        x = xs[i % 2]
+        _lib.check(lib.eva_moe_route(ctypes.byref(shape), x.data_ptr(), 1, M, layer.router_w.data_ptr(), bias.data_ptr(),
+                                     None, idx.data_ptr(), w.data_ptr(), ws.data_ptr(), ws.numel(), stream), "route")
+        if ev is not None:
+            ev[0].record()
+        _lib.check(lib.eva_moe_experts_prefill(ctypes.byref(shape), x.data_ptr(), 1, M, idx.data_ptr(), 0, w.data_ptr(),
+                                               tables, shared, ws.data_ptr(), ws.numel(), None, out.data_ptr(), stream),
+                   "experts_prefill")
+        if ev is not None:
+            ev[1].record()
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    loads = np.bincount(idx.cpu().numpy().ravel(), minlength=cfg.n_experts)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for i in range(steps):
+        step(i, evs[i])
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    ems = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    flop_exp = 6.0 * cfg.hidden * (M * cfg.topk * cfg.inter + M * cfg.shared_inter)
+    flop_router = 2.0 * M * cfg.hidden * cfg.n_experts
+    peak, kind = tensor_peak()
+    share = np.sort(loads)[::-1] / loads.sum()
+    return {"metric": "moe_layer_prefill_tokens_per_s", "value": M / (ms * 1e-3), "unit": "tokens/s",
+            "tokens_per_step": M, "ms_per_step": ms, "steps": steps,
+            "routing": f"router bias + {ZIPF_BETA} * log(rank^-{ZIPF_S}) (Zipf-skewed); expert load top-8 share "
+                       f"{share[:8].sum():.3f}, top-32 {share[:32].sum():.3f}, experts used {(loads > 0).sum()}",
+            "roofline": {"bound": "tensor", "achieved": (flop_exp) / (ems * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (flop_exp) / (ems * 1e-3) / 1e12 / peak, "peak_kind": kind,
+                         "kernel": "eva_moe_experts_prefill (permute + rotate + gate/up + down + combine)",
+                         "alg_flop_per_launch": flop_exp, "launch_ms": ems},
+            "step_tflops_incl_router": (flop_exp + flop_router) / (ms * 1e-3) / 1e12}
 
 
 class ClockSampler:
@@ -200,6 +288,12 @@ def main():
     cfg = CONFIGS[args.config]
     if args.small:
         cfg = cfg.with_(n_experts=64, n_group=8, topk_group=4)
+    if args.prefill_only:
+        layer = make_layer(cfg, dev, seed=0)
+        res = prefill_measure(cfg, layer, dev, max(1, min(args.steps, 10)), 2, args.prefill_tokens)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
     M = args.batch
     steps, warmup = args.steps, max(3, args.warmup)
     layer = make_layer(cfg, dev, seed=0)
@@ -340,6 +434,12 @@ def main():
                "sample": f"{len(ts)} single-token steps (FP64 router + top-{cfg.topk} routed experts + shared, "
                          f"EXL3 dequantised by the C restatement)"}
 
+    prefill = None
+    if not args.no_prefill and world == 1:
+        del moe
+        torch.cuda.empty_cache()
+        prefill = prefill_measure(cfg, layer, dev, max(1, min(steps, 10)), 2, args.prefill_tokens)
+
     tokens = M * steps * world
     line = {
         "metric": METRIC, "value": tokens / (ms_total * 1e-3), "unit": UNIT, "n_gpus": world, "steps": steps,
@@ -362,6 +462,7 @@ def main():
         "gpu_launches": 4 * steps,
         "clocks": clock_summary,
         "device_status": st,
+        "prefill": prefill,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -4,7 +4,7 @@
 // [rows x H] x [H x I] problem. Per CTA one 128-row x 128-column output tile:
 //   warp 0      producer: 2-D TMA loads (128B swizzle, no multicast) of the rotated input rows
 //               and 1-D bulk copies of the EXL3 trellis rows of the k-block into a 5-stage ring
-//   warps 2-9   decoders: EXL3 decode of the k-block's 32 weight tiles (exact fp16, one rounding)
+//   warps 2-17  decoders: EXL3 decode of the k-block's 32 weight tiles (exact fp16, one rounding)
 //               straight into the UMMA K-major 128B-swizzled shared-memory layout
 //   warp 1      one thread issues tcgen05.mma (M=128, N=128, K=16, fp16 x fp16 -> fp32 in TMEM)
 //               and commits each stage back to the producer through an mbarrier
@@ -31,7 +31,7 @@ namespace eva {
 
 constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;
 constexpr int PF_STAGES = 5;
-constexpr int PF_DEC = 8;                                // decoder warps
+constexpr int PF_DEC = 16;                               // decoder warps
 constexpr int NT_PF = 8;                                 // 16-column tiles per 128-column chunk
 constexpr int PF_THREADS = (2 + PF_DEC) * 32;
 constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB
@@ -274,9 +274,9 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, uint
             __syncwarp();
         }
     } else {
-        // decoders: warp d (0..7) takes k-tile row d / 2 of the block and tiles 4 (d % 2) .. +3
+        // decoders: warp d (0..15) takes k-tile row d / 4 of the block and tiles 2 (d % 4) .. +1
         const int d = warp - 2;
-        const int ktl = d >> 1, nt0 = (d & 1) * 4;
+        const int ktl = d >> 2, nt0 = (d & 3) * 2;
         const LaneDec ld = lane_dec<K>(lane);
         const int n0 = lane >> 2, k0 = 2 * (lane & 3);
         for (int s = 0; s < total; ++s) {
@@ -287,7 +287,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, uint
             const uint32_t* tr = reinterpret_cast<const uint32_t*>(stage + PF_A_BYTES + PF_B_BYTES + ktl * TROW);
             uint8_t* bt = stage + PF_A_BYTES;
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
+            for (int t = 0; t < 2; ++t) {
                 uint32_t a[4];
                 decode_afrag<K>(tr + (nt0 + t) * 8 * K, ld, a);
                 const int n = (nt0 + t) * 16 + n0;   // output column within the chunk (B row)
@@ -370,9 +370,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, con
     __shared__ PfSmem S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     PfTile t;
-    if (!pf_tile(p, blockIdx.x, t)) return;
+    if (!pf_tile(p, blockIdx.y, t)) return;
     const int I_e = t.shared ? p.I_sh : p.I;
-    const int chunk = blockIdx.y;
+    const int chunk = blockIdx.x;   // chunks of one row tile run next to each other: its rows stay in L2
     if (chunk * 128 >= I_e) return;
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
@@ -434,9 +434,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_down(const PfParams p, const
     __shared__ PfSmem S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     PfTile t;
-    if (!pf_tile(p, blockIdx.x, t)) return;
+    if (!pf_tile(p, blockIdx.y, t)) return;
     const int I_e = t.shared ? p.I_sh : p.I;
-    const int chunk = blockIdx.y;
+    const int chunk = blockIdx.x;
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
     pf_setup(S, warp, 128);
@@ -624,8 +624,8 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     // tile upper bound: sum over experts of ceil(n_e / 128) <= S / 128 + E, plus the shared tiles
     const int max_tiles = (p.S_cap + PF_BM - 1) / PF_BM + p.n_local + (p.has_shared ? (p.M + PF_BM - 1) / PF_BM : 0);
     const int imax_ch = L.imax / 128;
-    kg<<<dim3(max_tiles, imax_ch), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
-    kd<<<dim3(max_tiles, p.H / 128), PF_THREADS, PF_SMEM, stream>>>(p, ma);
+    kg<<<dim3(imax_ch, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
+    kd<<<dim3(p.H / 128, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, ma);
     const long long comb = static_cast<long long>(p.M) * (p.H / 128);
     pf_combine<<<static_cast<unsigned>((comb + 7) / 8), 256, 0, stream>>>(p);
     return cudaGetLastError();
