@@ -16,8 +16,11 @@ roofline  the fused experts launch (eva_moe_experts: permutation + experts kerne
 cpu_baseline  the CPU oracle port (C restatement + numpy router) on the host cores, rank 0, N = 1,
           on a bounded sample of the same workload.
 
-N > 1 (torchrun): every rank runs its own replica of the layer with its own token batches
-(replicas, weak scaling); value = all ranks' tokens / max over ranks of the timed region.
+N > 1 (torchrun): expert parallelism. Each rank holds n_experts / N experts (placed by expected
+load) and its own batch of --batch tokens (weak scaling; global batch N * batch); a step is
+EPMoE.forward (route, dispatch, NCCL exchange of rows, shared + local experts, exchange of partial
+sums back, combine). value = all ranks' tokens / max over ranks of the timed region. The prefill
+leg runs --prefill-tokens tokens per rank the same way with exact splits.
 
 --impl reference: the reference's CPU path restated (oracle port) on the host cores, rank 0 only.
 """
@@ -53,6 +56,8 @@ def parse():
     ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-only", action="store_true")
+    ap.add_argument("--ep-transport", default="peers", choices=["peers", "nccl"],
+                    help="N > 1: rows exchanged through NVLink peer memory by this library's kernels, or NCCL")
     return ap.parse_args()
 
 
@@ -264,6 +269,192 @@ def run_reference(args):
     }), flush=True)
 
 
+EXCHANGE = {
+    "peers": "NVLink peer memory (CUDA IPC arenas): dispatch kernel stores rows into the destinations' segments, "
+             "flags released per source, combine kernel reads the peers' FP32 partial rows; no host sync, no NCCL",
+    "nccl": "fixed segments (no host sync): grouped NCCL send/recv of rows, ids, weights; all-to-all of FP32 "
+            "partial sums back",
+}
+
+
+def zipf_load(cfg, seed=3):
+    """Expected relative load per expert under zipf_bias (rank^-s with the same rank permutation)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    rank = np.empty(cfg.n_experts)
+    rank[rng.permutation(cfg.n_experts)] = np.arange(1, cfg.n_experts + 1)
+    return rank ** -ZIPF_S
+
+
+def _max_over_ranks(v, dev):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def ep_bench(args, cfg, dev, rank, world, local):
+    """N > 1: expert parallelism. Each rank holds n_experts / N experts (placed by expected load) and
+    its own batch of tokens (weak scaling); the step is EPMoE.forward: route, dispatch, NCCL
+    exchange, shared + local experts, exchange back, combine."""
+    import dataclasses
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from eva_b200.ep import EPMoE, ExpertPlacement
+    from eva_b200.experts import make_layer
+
+    pl = ExpertPlacement.balanced(zipf_load(cfg), world)
+    layer = make_layer(cfg, dev, seed=0, experts=pl.experts_of(rank))
+    owner = torch.as_tensor(pl.owner, dtype=torch.int64)
+    M = args.batch
+    steps, warmup = args.steps, max(3, args.warmup)
+    nb = steps + warmup
+    routed_rec = 3 * cfg.hidden * cfg.inter * cfg.bits // 8 + 6 * (cfg.hidden + cfg.inter)
+    shared_rec = (3 * cfg.hidden * cfg.shared_inter * cfg.shared_bits // 8 + 6 * (cfg.hidden + cfg.shared_inter)
+                  if cfg.shared_inter else 0)
+    line = None
+    if not args.prefill_only:
+        ep = EPMoE(layer, pl, max_tokens=M, mode="fixed", transport=args.ep_transport)
+        g = torch.Generator(device=dev)
+        g.manual_seed(1 + rank)
+        xs = torch.randn(nb, M, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        idx_all = torch.empty(nb, M, cfg.topk, dtype=torch.int32, device=dev)
+        clocks = ClockSampler(local).__enter__()
+        clocks.wait_first()
+        for i in range(warmup):
+            ep.forward(xs[i], out=out, idx_out=idx_all[i])
+        torch.cuda.synchronize()
+        dist.barrier()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        torch.cuda.synchronize()
+        dist.barrier()
+        c_start = clocks.mark()
+        evs[0].record()
+        for i in range(steps):
+            ep.forward(xs[warmup + i], out=out, idx_out=idx_all[warmup + i])
+            evs[i + 1].record()
+        torch.cuda.synchronize()
+        time.sleep(0.06)
+        c_end = clocks.mark()
+        dist.barrier()
+        ms_total = _max_over_ranks(evs[0].elapsed_time(evs[-1]), dev)
+        step_ms = [evs[i].elapsed_time(evs[i + 1]) for i in range(steps)]
+        st = ep.status()
+        # algorithmic bytes of this rank: its experts that any rank's tokens selected, + the shared expert
+        gathered = [torch.empty_like(idx_all) for _ in range(world)]
+        dist.all_gather(gathered, idx_all)
+        allidx = torch.stack(gathered, 1).cpu().to(torch.int64)          # [nb, world, M, k]
+        U = [int(((owner[allidx[warmup + i].unique()] == rank)).sum()) for i in range(steps)]
+        alg = [u * routed_rec + shared_rec for u in U]
+        achieved = statistics.mean(b / (ms * 1e-3) for b, ms in zip(alg, step_ms)) / 1e9
+        achieved = _max_over_ranks(achieved, dev)
+        # end to end: pinned host batch in, BF16 result out, inside the timed region
+        xh = xs.cpu().pin_memory()
+        oh = torch.empty(M, cfg.hidden, dtype=torch.bfloat16).pin_memory()
+        xdev = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        for i in range(warmup):
+            xdev.copy_(xh[i], non_blocking=True)
+            oh.copy_(ep.forward(xdev, out=out), non_blocking=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            xdev.copy_(xh[warmup + i], non_blocking=True)
+            oh.copy_(ep.forward(xdev, out=out), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dev)
+        clocks.__exit__(None, None, None)
+        clock_summary = clocks.summary(c_start, c_end)
+        if not clock_summary["samples"]:
+            clock_summary = dict(clocks.summary(), note="timed region shorter than the 50 ms sampling period; "
+                                                        "samples from warm-up through e2e")
+        st = int(_max_over_ranks(st, dev))
+        peak, peak_kind = peaks()
+        tokens = M * steps * world
+        line = {
+            "metric": METRIC, "value": tokens / (ms_total * 1e-3), "unit": UNIT, "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms_total / steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp16 (EXL3 K3 weights decoded to fp16, fp32 accumulate), bf16 in/out",
+            "data": "synthetic (seeded random EXL3 trellis codes, N(0,1) bf16 hidden states)",
+            "config": {"workload": f"DeepSeek-{cfg.name.upper()} MoE layer decode (EXL3 K{cfg.bits}), batch {M} "
+                                   f"tokens/step per GPU, expert parallel over {world} GPUs"
+                                   + (" [small]" if args.small else ""),
+                       "hidden": cfg.hidden, "experts": cfg.n_experts, "experts_per_gpu": layer.n_local,
+                       "topk": cfg.topk, "inter": cfg.inter, "shared_inter": cfg.shared_inter, "bits": cfg.bits,
+                       "batch": M, "global_batch": M * world, "parallelism": f"ep{world}",
+                       "exchange": EXCHANGE[args.ep_transport],
+                       "l2": "inputs larger than L2 (4.24 GB experts over the ranks, new routes every step)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "whole EP step per rank (bytes: this rank's selected experts + shared, "
+                                   "max over ranks)",
+                         "distinct_local_experts_per_step": statistics.mean(U)},
+            "cpu_baseline": None,
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": M * cfg.hidden * 2,
+                    "d2h_bytes_per_step": M * cfg.hidden * 2},
+            "gpu_launches": (12 if args.ep_transport == "peers" else 9) * steps,
+            "clocks": clock_summary,
+            "device_status": st,
+        }
+        ep.close()
+        del ep, xs
+        torch.cuda.empty_cache()
+
+    prefill = None
+    if not args.no_prefill:
+        P = args.prefill_tokens
+        player = dataclasses.replace(layer, router_b=zipf_bias(cfg, layer.router_b))
+        ep = EPMoE(player, pl, max_tokens=P, mode="exact", transport=args.ep_transport)
+        g = torch.Generator(device=dev)
+        g.manual_seed(11 + rank)
+        xs = [torch.randn(P, cfg.hidden, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
+        out = torch.empty(P, cfg.hidden, dtype=torch.bfloat16, device=dev)
+        idx = torch.empty(P, cfg.topk, dtype=torch.int32, device=dev)
+        for i in range(2):
+            ep.forward(xs[i % 2], out=out, idx_out=idx)
+        torch.cuda.synchronize()
+        dist.barrier()
+        psteps = max(1, min(steps, 10))
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for i in range(psteps):
+            ep.forward(xs[i % 2], out=out)
+        t1.record()
+        torch.cuda.synchronize()
+        pms = _max_over_ranks(t0.elapsed_time(t1) / psteps, dev)
+        pst = int(_max_over_ranks(ep.status(), dev))
+        flop = 6.0 * cfg.hidden * (P * world * cfg.topk * cfg.inter + P * world * cfg.shared_inter)
+        peak, kind = tensor_peak()
+        achieved = flop / world / (pms * 1e-3) / 1e12
+        prefill = {"metric": "moe_layer_prefill_tokens_per_s", "value": P * world / (pms * 1e-3), "unit": "tokens/s",
+                   "tokens_per_step": P * world, "tokens_per_gpu": P, "ms_per_step": pms, "steps": psteps,
+                   "parallelism": f"ep{world}", "device_status": pst,
+                   "routing": f"router bias + {ZIPF_BETA} * log(rank^-{ZIPF_S}) (Zipf-skewed); experts placed on "
+                              f"ranks by expected load",
+                   "exchange": EXCHANGE[args.ep_transport] if args.ep_transport == "peers" else
+                               "exact splits (counts all-to-all + one host sync), grouped NCCL send/recv of rows, "
+                               "all-to-all of FP32 partial sums back",
+                   "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                                "frac": achieved / peak, "peak_kind": kind,
+                                "kernel": "whole EP prefill step per rank (routed + shared expert FLOPs / N)"}}
+        ep.close()
+        del ep
+        torch.cuda.empty_cache()
+    if line is None:
+        line = prefill
+    else:
+        line["prefill"] = prefill
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -288,6 +479,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.small:
         cfg = cfg.with_(n_experts=64, n_group=8, topk_group=4)
+    if world > 1:
+        return ep_bench(args, cfg, dev, rank, world, local)
     if args.prefill_only:
         layer = make_layer(cfg, dev, seed=0)
         res = prefill_measure(cfg, layer, dev, max(1, min(args.steps, 10)), 2, args.prefill_tokens)

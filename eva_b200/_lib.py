@@ -19,7 +19,11 @@ ACT_CLAMP_AFTER, ACT_CLAMP_BEFORE = 0, 1
 # every symbol include/eva_moe.h declares
 EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_status", "eva_moe_route",
            "eva_moe_topk", "eva_moe_permute", "eva_moe_experts", "eva_moe_forward", "eva_exl3_dequant",
-           "eva_moe_arch", "eva_moe_experts_noalloc", "eva_moe_experts_decode", "eva_moe_experts_prefill")
+           "eva_moe_arch", "eva_moe_experts_noalloc", "eva_moe_experts_decode", "eva_moe_experts_prefill",
+           "eva_ep_dispatch", "eva_ep_combine", "eva_ep_arena_layout", "eva_peer_alloc", "eva_peer_open",
+           "eva_peer_close", "eva_peer_free", "eva_ep_dispatch_peers", "eva_ep_wait_rows", "eva_ep_signal_partials",
+           "eva_ep_combine_peers")
+EP_MAX_WORLD = 32
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
 
@@ -38,6 +42,14 @@ def shape_of(cfg: MoEConfig, *, shared: bool = True, bits: int | None = None, li
                        cfg.bits if bits is None else bits, cfg.shared_inter if shared else 0, cfg.shared_bits,
                        cfg.router_code, cfg.n_group, cfg.topk_group, int(cfg.norm_topk), act_routed, act_shared,
                        float(cfg.route_scale), float(cfg.swiglu_limit if limit is None else limit))
+
+
+class EvaEpPeers(ctypes.Structure):
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("H", ctypes.c_int32), ("topk", ctypes.c_int32),
+                ("n_experts", ctypes.c_int32), ("segment_rows", ctypes.c_int32), ("x_elem_bytes", ctypes.c_int32),
+                ("reserved", ctypes.c_int32), ("off_x", ctypes.c_uint64), ("off_sel", ctypes.c_uint64),
+                ("off_rw", ctypes.c_uint64), ("off_part", ctypes.c_uint64), ("bytes", ctypes.c_uint64),
+                ("arena", ctypes.c_void_p * EP_MAX_WORLD), ("owner", ctypes.c_void_p), ("local_id", ctypes.c_void_p)]
 
 
 _lib = None
@@ -81,6 +93,19 @@ def load(build_if_missing: bool = True):
     L.eva_exl3_dequant.argtypes = [vp, i32, i32, i32, vp, vp]
     L.eva_moe_experts_noalloc.restype = ctypes.c_int
     L.eva_moe_experts_noalloc.argtypes = [shp, vp, i32, i32, vp, i32, vp, P(vp), P(ctypes.c_int64), vp, vp, vp, vp]
+    L.eva_ep_dispatch.restype = ctypes.c_int
+    L.eva_ep_dispatch.argtypes = [i32, i32, i32, vp, i32, i32, vp, vp, i32, vp, vp, i32, i32, vp, vp, vp, vp, vp, vp, vp]
+    L.eva_ep_combine.restype = ctypes.c_int
+    L.eva_ep_combine.argtypes = [i32, i32, i32, vp, vp, vp, vp, vp, vp]
+    pp = P(EvaEpPeers)
+    for name, args in (("eva_ep_arena_layout", [pp]), ("eva_peer_alloc", [sz, P(vp), vp]), ("eva_peer_open", [vp, P(vp)]),
+                       ("eva_peer_close", [vp]), ("eva_peer_free", [vp]),
+                       ("eva_ep_dispatch_peers", [pp, vp, i32, vp, vp, vp, vp, vp, vp]),
+                       ("eva_ep_wait_rows", [pp, vp, vp]), ("eva_ep_signal_partials", [pp, vp]),
+                       ("eva_ep_combine_peers", [pp, i32, vp, vp, vp, vp, vp, vp])):
+        fn = getattr(L, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = args
     L.eva_moe_arch.restype = i32
     L.eva_moe_arch.argtypes = []
     _lib = L

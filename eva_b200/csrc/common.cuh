@@ -30,7 +30,7 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p)
 }
 
 // ---------------------------------------------------------------------------------------------
-// mbarrier + bulk copy (TMA, 1-D, no multicast)
+// mbarrier + bulk copy (TMA, 1-D, one CTA per copy)
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
 {

@@ -11,8 +11,8 @@
 // chunks, then all down chunks). An item only ever waits (bounded) on items with smaller indices,
 // which were claimed earlier by running CTAs, so the schedule cannot deadlock.
 //
-// Per CTA: 1 producer warp streams the item's trellis rows with 1-D bulk copies (TMA, no
-// multicast) into a 4-stage shared-memory ring (32 k-tile rows x 128 columns per stage); 16
+// Per CTA: 1 producer warp streams the item's trellis rows with 1-D bulk copies (TMA, one
+// CTA per copy) into a 4-stage shared-memory ring (32 k-tile rows x 128 columns per stage); 16
 // consumer warps each decode 4 rows x 4 tiles per stage in registers and run mma.m16n8k16 with
 // the weights as the 16 x 16 A operand (rows = output columns) and up to 8 tokens as the B
 // operand, accumulating in fp32. The MMA takes the raw codebook values h = 1024 + bytesum and the

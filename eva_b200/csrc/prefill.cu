@@ -2,7 +2,7 @@
 //
 // Tokens are grouped by expert (the permutation's sorted order), so each expert is a dense
 // [rows x H] x [H x I] problem. Per CTA one 128-row x 128-column output tile:
-//   warp 0      producer: 2-D TMA loads (128B swizzle, no multicast) of the rotated input rows
+//   warp 0      producer: 2-D TMA loads (128B swizzle, plain per-CTA loads) of the rotated input rows
 //               and 1-D bulk copies of the EXL3 trellis rows of the k-block into a 5-stage ring
 //   warps 2-17  decoders: EXL3 decode of the k-block's 32 weight tiles (exact fp16, one rounding)
 //               straight into the UMMA K-major 128B-swizzled shared-memory layout

@@ -464,13 +464,18 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
             const int n = a.tok_expect[m] + (a.has_shared ? 1 : 0);
             a.tok_expect[m] = n;
         }
+        __syncthreads();
         if (!a.has_shared) {
-            for (int i = tid; i < a.M * a.H; i += PERM_THREADS) {
-                const int m = i / a.H;
-                if (a.tok_expect[m] == 0) {
-                    if (a.out_f32) a.out_f32[i] = 0.0f;
-                    if (a.out_bf16) static_cast<__nv_bfloat16*>(a.out_bf16)[i] = __float2bfloat16_rn(0.0f);
-                }
+            // warp per row; only rows without arrivals are written (H is a multiple of 256)
+            for (int m = warp; m < a.M; m += PERM_THREADS / 32) {
+                if (a.tok_expect[m] != 0) continue;
+                const size_t row = static_cast<size_t>(m) * a.H;
+                if (a.out_f32)
+                    for (int c = lane * 4; c < a.H; c += 128)
+                        *reinterpret_cast<float4*>(a.out_f32 + row + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (a.out_bf16)   // 8-byte aligned
+                    for (int c = lane * 4; c < a.H; c += 128)
+                        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out_bf16) + row + c) = make_uint2(0, 0);
             }
         }
     }

@@ -63,17 +63,23 @@ class ExpertLayer:
     shared: torch.Tensor | None    # int64 [9] addresses of the shared expert
     router_w: torch.Tensor         # float32 [E, H]
     router_b: torch.Tensor         # float32 [E] (e_score_correction_bias / gate bias)
+    experts: tuple = ()            # global ids of the routed records held, in table order
 
     @property
     def device(self):
         return self.storage.device
+
+    @property
+    def n_local(self) -> int:
+        """Routed experts held (columns of `packed`); equals cfg.n_experts for a whole layer."""
+        return len(self.experts)
 
     def tensor(self, expert: int, proj: str, kind: str) -> torch.Tensor:
         """View of one tensor of a routed expert (expert == -1: the shared expert)."""
         cfg = self.cfg
         if expert < 0:
             offs, _, shapes = record_layout(cfg.hidden, cfg.shared_inter, cfg.shared_bits)
-            base = cfg.n_experts * self.record_bytes
+            base = self.n_local * self.record_bytes
             bits = cfg.shared_bits
         else:
             offs, _, shapes = record_layout(cfg.hidden, cfg.inter, cfg.bits)
@@ -95,17 +101,17 @@ class ExpertLayer:
         return _with_storage(self, self.storage.to(device), device)
 
 
-def _pointer_tables(cfg: MoEConfig, storage: torch.Tensor, record_bytes: int):
+def _pointer_tables(cfg: MoEConfig, storage: torch.Tensor, record_bytes: int, n_local: int):
     base = storage.data_ptr()
     offs, _, _ = record_layout(cfg.hidden, cfg.inter, cfg.bits)
-    packed = torch.zeros(PTR_ROWS, cfg.n_experts, dtype=torch.int64)
+    packed = torch.zeros(PTR_ROWS, n_local, dtype=torch.int64)
     for (proj, kind), row in ROW.items():
         off = offs[(proj, kind)][0]
-        packed[row] = base + off + torch.arange(cfg.n_experts, dtype=torch.int64) * record_bytes
+        packed[row] = base + off + torch.arange(n_local, dtype=torch.int64) * record_bytes
     shared = None
     if cfg.shared_inter:
         soffs, _, _ = record_layout(cfg.hidden, cfg.shared_inter, cfg.shared_bits)
-        sbase = base + cfg.n_experts * record_bytes
+        sbase = base + n_local * record_bytes
         shared = torch.zeros(PTR_ROWS, dtype=torch.int64)
         for (proj, kind), row in ROW.items():
             shared[row] = sbase + soffs[(proj, kind)][0]
@@ -113,11 +119,11 @@ def _pointer_tables(cfg: MoEConfig, storage: torch.Tensor, record_bytes: int):
 
 
 def _with_storage(layer: ExpertLayer, storage: torch.Tensor, device=None) -> ExpertLayer:
-    packed, shared = _pointer_tables(layer.cfg, storage, layer.record_bytes)
+    packed, shared = _pointer_tables(layer.cfg, storage, layer.record_bytes, layer.n_local)
     dev = storage.device
     return ExpertLayer(layer.cfg, storage, layer.record_bytes, packed.to(dev),
                        None if shared is None else shared.to(dev),
-                       layer.router_w.to(dev), layer.router_b.to(dev))
+                       layer.router_w.to(dev), layer.router_b.to(dev), layer.experts)
 
 
 def _fill_record(storage, base, offs, shapes, gen, scale, device):
@@ -134,31 +140,42 @@ def _fill_record(storage, base, offs, shapes, gen, scale, device):
             storage[base + o: base + o + b].view(torch.float16).copy_((sign * jit * mag).to(torch.float16))
 
 
+def _record_seed(seed: int, index: int) -> int:
+    return (seed * 1_000_003 + index + 1) & 0x7FFF_FFFF_FFFF_FFFF
+
+
 def make_layer(cfg: MoEConfig, device="cpu", seed: int = 0, svh_scale: float = 0.02,
                router_scale: float = 0.02, bias_std: float | None = None,
-               n_fill: int | None = None) -> ExpertLayer:
+               n_fill: int | None = None, experts=None) -> ExpertLayer:
     """Synthetic layer: seeded EXL3 experts (+ shared expert), FP32 router weights and bias.
 
-    Seeds follow one rule: weights from `seed`, router bias from `seed + 2`.
-    n_fill: fill only the first n_fill routed experts with random data (the rest stay zero, a
-    valid all-zero-state code); used to build multi-GB layers quickly.
+    Seeds: routed expert e from (seed, e), the shared expert from (seed, n_experts), router weights
+    from `seed`, router bias from `seed + 2`. Each record has its own seed stream, so a layer built
+    for a subset of experts (one expert-parallel rank) holds exactly the bytes of the whole layer.
+    experts: global ids of the routed experts to hold, in table order (default: all).
+    n_fill: fill only the first n_fill held experts with random data (the rest stay zero, a valid
+    all-zero-state code); used to build multi-GB layers quickly.
     """
     device = torch.device(device)
+    ids = tuple(range(cfg.n_experts)) if experts is None else tuple(int(e) for e in experts)
+    if any(not 0 <= e < cfg.n_experts for e in ids) or len(set(ids)) != len(ids):
+        raise ValueError("experts must be distinct ids in [0, n_experts)")
     _, rec, _ = record_layout(cfg.hidden, cfg.inter, cfg.bits)
-    total = cfg.n_experts * rec
+    total = len(ids) * rec
     if cfg.shared_inter:
         _, srec, _ = record_layout(cfg.hidden, cfg.shared_inter, cfg.shared_bits)
         total += srec
     storage = torch.zeros(total, dtype=torch.uint8, device=device)
     gen = torch.Generator(device=device)
-    gen.manual_seed(seed)
     offs, _, shapes = record_layout(cfg.hidden, cfg.inter, cfg.bits)
-    nf = cfg.n_experts if n_fill is None else min(n_fill, cfg.n_experts)
-    for e in range(nf):
-        _fill_record(storage, e * rec, offs, shapes, gen, svh_scale, device)
+    nf = len(ids) if n_fill is None else min(n_fill, len(ids))
+    for i in range(nf):
+        gen.manual_seed(_record_seed(seed, ids[i]))
+        _fill_record(storage, i * rec, offs, shapes, gen, svh_scale, device)
     if cfg.shared_inter:
         soffs, _, sshapes = record_layout(cfg.hidden, cfg.shared_inter, cfg.shared_bits)
-        _fill_record(storage, cfg.n_experts * rec, soffs, sshapes, gen, svh_scale, device)
+        gen.manual_seed(_record_seed(seed, cfg.n_experts))
+        _fill_record(storage, len(ids) * rec, soffs, sshapes, gen, svh_scale, device)
     rgen = torch.Generator(device="cpu")
     rgen.manual_seed(seed)
     router_w = (torch.randn(cfg.n_experts, cfg.hidden, generator=rgen) * router_scale).to(device)
@@ -167,15 +184,15 @@ def make_layer(cfg: MoEConfig, device="cpu", seed: int = 0, svh_scale: float = 0
     if bias_std is None:
         bias_std = 0.01 if cfg.router != "softmax" else 0.0
     router_b = (torch.randn(cfg.n_experts, generator=bgen) * bias_std).to(device)
-    packed, shared = _pointer_tables(cfg, storage, rec)
+    packed, shared = _pointer_tables(cfg, storage, rec, len(ids))
     return ExpertLayer(cfg, storage, rec, packed.to(device), None if shared is None else shared.to(device),
-                       router_w, router_b)
+                       router_w, router_b, ids)
 
 
 def replicate_experts(layer: ExpertLayer, n_src: int) -> None:
     """Copy the first n_src routed records cyclically over the remaining experts (in place)."""
     rec = layer.record_bytes
-    E = layer.cfg.n_experts
+    E = layer.n_local
     src = layer.storage[: n_src * rec]
     for e in range(n_src, E, n_src):
         n = min(n_src, E - e)

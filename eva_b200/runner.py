@@ -166,6 +166,8 @@ class EvaMoE:
     def __init__(self, layer: ExpertLayer, max_rows: int = 64):
         if not torch.cuda.is_available() or layer.device.type != "cuda":
             raise RuntimeError("EvaMoE requires a CUDA-resident ExpertLayer; there is no CPU fallback")
+        if layer.n_local != layer.cfg.n_experts:
+            raise ValueError("EvaMoE needs every routed expert; use eva_b200.ep.EPMoE for an expert shard")
         self.lib = _lib.load()
         self.layer = layer
         self.cfg: MoEConfig = layer.cfg

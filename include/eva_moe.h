@@ -162,6 +162,91 @@ int eva_moe_experts_noalloc(const EvaMoeShape* shape, const void* x, int32_t x_i
                             const int64_t* const* tables, const int64_t* shared,
                             float* out_f32, void* out_bf16, int32_t* status_out, void* stream);
 
+/* ---- expert parallelism (one process per GPU; the exchange itself is NCCL all-to-all) ----------
+ * No counterpart in the reference, which has no expert parallelism: these replace the kernel-side
+ * local-expert filter slot_info (runtime/ds41/csrc/moe_coop2048/vendor/exl3_moe_coop_kernel.cuh:208-223)
+ * and the empty-row path write_empty_row_chunk (:573-610) with an explicit dispatch and combine.
+ *
+ * eva_ep_dispatch: plan and pack the rows this rank sends. Token m goes to rank r once when at least
+ * one of its slots with a non-zero weight has an expert owned by r.
+ *   x:            [M][H] rows of x_elem_bytes (2: bf16/fp16, 4: fp32) elements, 16-byte aligned
+ *   idx, w:       int32 / float [M][topk] global expert ids and routing weights (eva_moe_route)
+ *   owner:        int32 [n_experts] rank holding each global expert; local_id: int32 [n_experts] the
+ *                 expert's column in that rank's pointer tables
+ *   segment_rows: 0 = rows for rank r packed after rank r-1's (exact splits: read counts on the host);
+ *                 > 0 = rank r's rows start at r * segment_rows, padding rows zeroed (fixed splits,
+ *                 no host synchronisation; needs segment_rows >= rows sent to any rank)
+ *   capacity:     rows in send_x / send_sel / send_rw (>= world * segment_rows in fixed mode;
+ *                 M * min(topk, world) always suffices in packed mode)
+ *   counts:       int32 [world] rows for each rank; pos: int32 [world][M] send row of (rank, token), -1 if none
+ *   send_sel/rw:  int32 / float [capacity][topk]: destination-local expert ids, and the weights with 0 for
+ *                 the slots whose expert is on another rank (inactive in eva_moe_experts)
+ *   status:       device int32 (may be NULL): EVA_STATUS_BAD_EXPERT for ids outside [0, n_experts) or
+ *                 owners outside [0, world); EVA_STATUS_CAPACITY when rows did not fit (they are dropped) */
+int eva_ep_dispatch(int32_t H, int32_t topk, int32_t n_experts, const void* x, int32_t x_elem_bytes, int32_t M,
+                    const int32_t* idx, const float* w, int32_t world, const int32_t* owner, const int32_t* local_id,
+                    int32_t capacity, int32_t segment_rows, int32_t* counts, int32_t* pos, void* send_x,
+                    int32_t* send_sel, float* send_rw, int32_t* status, void* stream);
+
+/* eva_ep_combine: out[m] = base[m] + sum over r = 0 .. world-1 (in that order) of back[pos[r][m]],
+ * skipping pos < 0. back: float [rows][H], the routed partial sums returned in send order;
+ * base: float [M][H] (the shared expert's output) or NULL; out_f32 / out_bf16 (at least one). */
+int eva_ep_combine(int32_t H, int32_t M, int32_t world, const float* back, const int32_t* pos,
+                   const float* base, float* out_f32, void* out_bf16, void* stream);
+
+/* ---- expert parallelism over NVLink peer memory (no collective library in the data path) -------
+ * Every rank owns one arena in its GPU memory, mapped into every other rank's process (CUDA IPC):
+ *   flags     epoch (this rank's step count), a block counter, the "partials ready" flag, and one
+ *             "rows ready" flag per source rank
+ *   recv_x    [world][segment_rows][H]   rows sent to this rank, source-major
+ *   recv_sel  int32 [world][segment_rows][topk], recv_rw float [same]: destination-local expert ids
+ *             and weights (0 for the slots of other ranks' experts and for padding rows)
+ *   part      float [world][segment_rows][H]: this rank's routed partial sums of the received rows
+ * A step: eva_ep_dispatch_peers (plan; each row stored straight into its destination's recv_*; the
+ * last block releases every destination's "rows ready" flag for this source) -> eva_ep_wait_rows
+ * -> eva_moe_experts on the recv_* rows into part -> eva_ep_signal_partials -> eva_ep_combine_peers
+ * (waits for every rank's "partials ready" flag, then reads the partial rows of this rank's tokens
+ * from the peers' arenas). Flags hold step numbers, so no reset is needed between steps, and a
+ * rank cannot overwrite a peer's rows before the peer has finished the previous step (its combine
+ * waited for that peer's partials). Every wait is bounded (2 s) and sets EVA_STATUS_TIMEOUT. */
+#define EVA_EP_MAX_WORLD 32
+
+typedef struct EvaEpPeers {
+    int32_t world, rank;              /* ranks, this rank */
+    int32_t H, topk, n_experts;       /* hidden size, slots per token, routed experts (global) */
+    int32_t segment_rows;             /* rows each source may send to each destination per step */
+    int32_t x_elem_bytes;             /* 2 (bf16 / fp16 rows) */
+    int32_t reserved;
+    uint64_t off_x, off_sel, off_rw, off_part, bytes;   /* arena layout: eva_ep_arena_layout fills these */
+    void* arena[EVA_EP_MAX_WORLD];    /* every rank's arena as mapped in this process (own included) */
+    const int32_t* owner;             /* device int32 [n_experts]: rank holding each expert */
+    const int32_t* local_id;          /* device int32 [n_experts]: its column in that rank's tables */
+} EvaEpPeers;
+
+/* Fill the off_* / bytes fields of *p from world, H, topk, segment_rows and x_elem_bytes. */
+int eva_ep_arena_layout(EvaEpPeers* p);
+
+/* Arena memory: allocate (zeroed) and export a 64-byte CUDA IPC handle; map a peer's handle; unmap;
+ * free. Setup-time calls (they allocate and synchronise), unlike every other entry point. */
+int eva_peer_alloc(size_t bytes, void** ptr, void* handle_out);
+int eva_peer_open(const void* handle, void** ptr);
+int eva_peer_close(void* ptr);
+int eva_peer_free(void* ptr);
+
+/* Plan + pack: token rows (x [M][H], routes idx/w [M][topk]) stored into the destinations' arenas.
+ * pos: int32 [world][M], the token's row within its segment at rank r (-1: not sent); counts: int32
+ * [world]. EVA_STATUS_CAPACITY when a destination would get more than segment_rows rows (dropped). */
+int eva_ep_dispatch_peers(const EvaEpPeers* p, const void* x, int32_t M, const int32_t* idx, const float* w,
+                          int32_t* counts, int32_t* pos, int32_t* status, void* stream);
+/* Wait until every source's rows of this step are in this rank's arena. */
+int eva_ep_wait_rows(const EvaEpPeers* p, int32_t* status, void* stream);
+/* Publish this rank's partial sums of this step (after the experts launch that wrote part). */
+int eva_ep_signal_partials(const EvaEpPeers* p, void* stream);
+/* out[m] = base[m] + sum over r (rank order) of rank r's partial row for token m; waits for every
+ * rank's partials first. base: float [M][H] or NULL; out_f32 / out_bf16 at least one. */
+int eva_ep_combine_peers(const EvaEpPeers* p, int32_t M, const int32_t* pos, const float* base, float* out_f32,
+                         void* out_bf16, int32_t* status, void* stream);
+
 /* Library identification: sm arch the kernels were built for (100 for sm_100a). */
 int32_t eva_moe_arch(void);
 

@@ -270,7 +270,8 @@ def moe_forward(x_bits: np.ndarray, sel: np.ndarray, rw: np.ndarray, layer, thre
     if with_shared and layer.shared is not None:
         sh = np.ascontiguousarray(layer.shared.numpy(), dtype=np.int64)
     out = np.empty((M, H), dtype=np.float32)
-    st = lib().eo_moe_forward(_ptr(x), int(x_is_f16), M, H, cfg.inter, cfg.topk, cfg.n_experts, _ptr(sel32), _ptr(rw32),
+    n_tab = ptrs.shape[0]
+    st = lib().eo_moe_forward(_ptr(x), int(x_is_f16), M, H, cfg.inter, cfg.topk, n_tab, _ptr(sel32), _ptr(rw32),
                               _ptr(ptrs), cfg.bits, None if sh is None else _ptr(sh),
                               cfg.shared_inter if sh is not None else 0, cfg.shared_bits,
                               float(cfg.swiglu_limit), _ptr(out), None, int(threads))
