@@ -648,7 +648,8 @@ def main():
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind, "kernel": "eva_moe_experts (permute + experts_kernel)",
                      "alg_bytes_per_launch": statistics.mean(alg_bytes), "launch_ms": statistics.mean(exp_ms),
-                     "distinct_experts_per_step": statistics.mean(U)},
+                     "distinct_experts_per_step": statistics.mean(U),
+                     "distinct_experts_by_batch": [int(len(np.unique(idx_host[i]))) for i in range(nb)]},
         "cpu_baseline": cpu,
         "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": M * cfg.hidden * 2,
                 "d2h_bytes_per_step": M * cfg.hidden * 2},
