@@ -69,18 +69,26 @@ __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_c
 // Bounded wait on an mbarrier phase. Returns false (and flags ST_TIMEOUT) when it gives up. Once
 // any wait of the launch has given up, later waits return at once, so a systematic failure costs
 // one wait limit, not one per stage.
+// try_wait suspends the thread in hardware for a while, so the loop is not hot; the clock and the
+// global status word are only read every 32 unsuccessful tries (a global load per try would put
+// every briefly waiting warp behind a memory round trip).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status)
 {
     if (mbar_try_wait(bar, parity)) return true;
-    if (ld_volatile(status) & ST_TIMEOUT) return false;
-    const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > WAIT_LIMIT_NS || (ld_volatile(status) & ST_TIMEOUT)) {
-            atomicOr(status, ST_TIMEOUT);
-            return false;
+    uint64_t t0 = 0;
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31) == 0) {
+            const uint64_t t = globaltimer();
+            if (t0 == 0) {
+                t0 = t;
+                if (ld_volatile(status) & ST_TIMEOUT) return false;
+            } else if (t - t0 > WAIT_LIMIT_NS || (ld_volatile(status) & ST_TIMEOUT)) {
+                atomicOr(status, ST_TIMEOUT);
+                return false;
+            }
         }
     }
-    return true;
 }
 
 // Global -> shared bulk copy completing on an mbarrier. dst, src 16-byte aligned, bytes % 16 == 0.
@@ -321,6 +329,20 @@ __device__ __forceinline__ void decode_raw(const uint32_t* tile, const LaneGrp& 
     a[1] = __byte_perm(h[4], h[5], 0x5410);
     a[2] = __byte_perm(h[2], h[3], 0x5410);
     a[3] = __byte_perm(h[6], h[7], 0x5410);
+}
+
+// A fragment from the lane's two trellis words (word w0 high, w1 low): exact fp16 weights.
+template <int K>
+__device__ __forceinline__ void decode_afrag_words(uint32_t w0, uint32_t w1, int off, uint32_t (&a)[4])
+{
+    const uint64_t v = (static_cast<uint64_t>(w0) << 32) | w1;
+    uint32_t st[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) st[j] = static_cast<uint32_t>(v >> (48 - off - j * K)) & 0xffffu;
+    a[0] = mul1_pair(st[0], st[1]);
+    a[1] = mul1_pair(st[4], st[5]);
+    a[2] = mul1_pair(st[2], st[3]);
+    a[3] = mul1_pair(st[6], st[7]);
 }
 
 // A fragment (4 x half2) of one tile for a lane: exact fp16 weights.

@@ -46,7 +46,7 @@ struct PermuteArgs {
     int32_t* runs;
     int32_t* run_expert;        // may be null
     int32_t* estart;            // may be null
-    int32_t* tstart;            // may be null: [E + 2] prefix of 128-row tiles per expert (+ shared)
+    int32_t* tstart;            // may be null: [E + 2] prefix of PF_TILE_ROWS-row tiles per expert (+ shared)
     int32_t* slot_act;          // may be null
     int32_t* tok_expect;        // may be null
     int32_t* counters;          // zeroed when non-null
@@ -75,6 +75,7 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream);
 cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream);
 
 constexpr int PREFILL_MIN_ROWS = 129;   // eva_moe_experts takes the tensor-core path from this many rows
+constexpr int PF_TILE_ROWS = 256;       // rows of one expert per tensor-core CTA (two 128-row MMA halves)
 
 // Permutation + fused experts on a caller-provided workspace laid out by ws_layout(shape, M, allow_split).
 int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,

@@ -1,18 +1,20 @@
 // Prefill-shaped MoE experts on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
 // Tokens are grouped by expert (the permutation's sorted order), so each expert is a dense
-// [rows x H] x [H x I] problem. Per CTA one 128-row x 128-column output tile:
+// [rows x H] x [H x I] problem. Per CTA up to 256 rows of one expert (two 128-row halves) x one
+// 128-column output chunk; both halves share every decoded weight tile:
 //   warp 0      producer: 2-D TMA loads (128B swizzle, plain per-CTA loads) of the rotated input rows
-//               and 1-D bulk copies of the EXL3 trellis rows of the k-block into a 5-stage ring
+//               of each half and 1-D bulk copies of the EXL3 trellis rows of the k-block into a
+//               4-stage ring
 //   warps 2-17  decoders: EXL3 decode of the k-block's 32 weight tiles (exact fp16, one rounding)
 //               straight into the UMMA K-major 128B-swizzled shared-memory layout
-//   warp 1      one thread issues tcgen05.mma (M=128, N=128, K=16, fp16 x fp16 -> fp32 in TMEM)
-//               and commits each stage back to the producer through an mbarrier
+//   warp 1      one thread issues tcgen05.mma (M=128 per half, N=128, K=16, fp16 x fp16 -> fp32 in
+//               TMEM) and commits each stage back to the producer through an mbarrier
 //   all warps   epilogue: tcgen05.ld of the accumulators, Hadamard / scales / activation in
 //               registers, fp16 or fp32 stores.
 // Kernels:
 //   pf_rotate    x -> fp16(H128(x * suh)) for gate and up, rows in expert-sorted order
-//   pf_gateup    gate and up accumulators (TMEM columns 0-127 / 128-255), epilogue = the MoE
+//   pf_gateup    gate and up accumulators (TMEM columns 128 (2 proj + half)), epilogue = the MoE
 //                coop A epilogue (exl3_moe_coop_kernel.cuh:758-808): H128, svh, SiLU*mul, suh_down,
 //                H128 -> fp16 down input
 //   pf_down      down projection, epilogue H128 * svh * routing weight -> per-slot fp32 rows
@@ -29,18 +31,28 @@
 
 namespace eva {
 
-constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;
-constexpr int PF_STAGES = 5;
+constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;   // PF_BM: rows of one MMA half
+constexpr int PF_HALVES = PF_TILE_ROWS / PF_BM;
 constexpr int PF_DEC = 16;                               // decoder warps
 constexpr int NT_PF = 8;                                 // 16-column tiles per 128-column chunk
-constexpr int PF_THREADS = (2 + PF_DEC) * 32;
-constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB
+constexpr int PF_THREADS = (3 + PF_DEC) * 32;            // A producer, MMA, 16 decoders, trellis producer
+constexpr int PF_TWARP = 2 + PF_DEC;                     // the trellis producer warp
+constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB per half
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;            // 16 KB
 constexpr int PF_T_BYTES = 4 * 8 * 32 * 4;               // 4 k-tile rows x 8 tiles x 32K bytes (K <= 4)
-constexpr int PF_STAGE = PF_A_BYTES + PF_B_BYTES + PF_T_BYTES;
+// three rings: activations (MMA operand A, both halves), trellis (decoder input), decoded weights
+// (MMA operand B). The trellis ring runs furthest ahead, so the decoders never wait on a TMA round
+// trip through the MMA; the decoders run up to PF_NB k-blocks ahead of the MMA.
+constexpr int PF_NA = 4, PF_NT = 8, PF_NB = 3;
+constexpr int PF_A_STAGE = PF_HALVES * PF_A_BYTES;
+constexpr int PF_OFF_B = PF_NA * PF_A_STAGE;
+constexpr int PF_OFF_T = PF_OFF_B + PF_NB * PF_B_BYTES;
+constexpr int PF_RING = PF_OFF_T + PF_NT * PF_T_BYTES;
 constexpr int PF_EPI_LD = 129;                           // padded row (floats) of the epilogue tiles
-constexpr size_t PF_SMEM = 1024 + static_cast<size_t>(PF_STAGES) * PF_STAGE + 256;
-static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PF_STAGES * PF_STAGE, "epilogue tiles reuse the ring");
+constexpr size_t PF_SMEM = 1024 + static_cast<size_t>(PF_RING) + 256;
+static_assert(PF_HALVES == 2, "two MMA halves per CTA");
+static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PF_RING, "epilogue tiles reuse the rings");
+static_assert(PF_SMEM <= 227 * 1024, "shared memory per CTA");
 
 struct PfParams {
     int M, H, I, I_sh, topk, S_cap, n_local, K, K_sh, has_shared, imax, act_routed, act_shared;
@@ -124,6 +136,19 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Explicit shared-space accesses for the decoders (generic accesses wait on the long scoreboard).
+__device__ __forceinline__ uint32_t lds32(uint32_t addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v)
+{
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // Byte offset of element (row, k) (k < 64, fp16) in a K-major 128B-swizzled 128 x 64 tile.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k)
 {
@@ -137,7 +162,7 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int k)
 struct PfTile {
     int e;         // expert, n_local = shared
     int row0;      // first sorted row of the tile
-    int rows;      // valid rows (<= 128)
+    int rows;      // valid rows (<= PF_TILE_ROWS)
     bool shared;
 };
 
@@ -149,8 +174,8 @@ __device__ __forceinline__ bool pf_tile(const PfParams& p, int mt, PfTile& t)
         t.e = E;
         t.shared = true;
         const int j = mt - p.tstart[E];
-        t.row0 = p.S_cap + j * PF_BM;
-        t.rows = min(PF_BM, p.M - j * PF_BM);
+        t.row0 = p.S_cap + j * PF_TILE_ROWS;
+        t.rows = min(PF_TILE_ROWS, p.M - j * PF_TILE_ROWS);
         return true;
     }
     int lo = 0, hi = E - 1;   // last e with tstart[e] <= mt
@@ -162,8 +187,8 @@ __device__ __forceinline__ bool pf_tile(const PfParams& p, int mt, PfTile& t)
     t.e = lo;
     t.shared = false;
     const int j = mt - p.tstart[lo];
-    t.row0 = p.estart[lo] + j * PF_BM;
-    t.rows = min(PF_BM, p.estart[lo + 1] - t.row0);
+    t.row0 = p.estart[lo] + j * PF_TILE_ROWS;
+    t.rows = min(PF_TILE_ROWS, p.estart[lo + 1] - t.row0);
     return true;
 }
 
@@ -215,7 +240,9 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
 
 // ---------------------------------------------------------------------------------------------
 // Shared main loop of the two GEMM kernels.
-//   nproj   projections accumulated (gate+up: 2, down: 1), each into its own 128 TMEM columns
+//   nproj   projections accumulated (gate+up: 2, down: 1); accumulator (proj, half) at TMEM
+//           columns 128 (proj * 2 + half)
+//   nh      halves with rows (1 or 2)
 //   nkb     k-blocks (64) per projection
 //   amaps   tensor maps of the A rows per projection; trellis bases per projection
 
@@ -224,52 +251,69 @@ struct PfLoop {
     const uint8_t* trellis[2];
     size_t row_stride;       // bytes between k-tile rows of the trellis
     int chunk;               // 128-column output chunk
-    int nproj, nkb, row0;
+    int nproj, nkb, row0, nh;
+};
+
+struct PfBars {
+    uint64_t afull[PF_NA], aempty[PF_NA], tfull[PF_NT], tempty[PF_NT], bfull[PF_NB], bempty[PF_NB], accb;
 };
 
 template <int K>
-__device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, uint64_t* full, uint64_t* dec, uint64_t* empty,
-                                            uint64_t* accb, uint32_t tmem, int warp, int lane, int* status)
+__device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBars& B, uint32_t tmem, int warp, int lane,
+                                            int* status)
 {
     const int total = L.nproj * L.nkb;
     constexpr uint32_t TROW = NT_PF * 32 * K;   // bytes of one k-tile row's 8 tiles
     if (warp == 0) {
-        // producer
+        // activation producer: both halves' rows of the k-block (2-D TMA)
         for (int s = 0; s < total; ++s) {
-            const int st = s % PF_STAGES;
-            const uint32_t ph = (s / PF_STAGES) & 1;
-            mbar_wait(&empty[st], ph ^ 1, status);
+            const int st = s % PF_NA;
+            mbar_wait(&B.aempty[st], ((s / PF_NA) & 1) ^ 1, status);
             const int pj = s / L.nkb, kb = s % L.nkb;
-            uint8_t* stage = ring + st * PF_STAGE;
             if (lane == 0) {
-                mbar_arrive_expect_tx(&full[st], PF_A_BYTES + 4 * TROW);
-                tma_load_2d(stage, L.amap[pj], kb * PF_BK, L.row0, &full[st]);
+                uint8_t* dst = ring + st * PF_A_STAGE;
+                mbar_arrive_expect_tx(&B.afull[st], L.nh * PF_A_BYTES);
+                for (int h = 0; h < L.nh; ++h)
+                    tma_load_2d(dst + h * PF_A_BYTES, pj ? L.amap[1] : L.amap[0], kb * PF_BK, L.row0 + h * PF_BM,
+                                &B.afull[st]);
             }
             __syncwarp();
+        }
+    } else if (warp == PF_TWARP) {
+        // trellis producer: the k-block's 4 k-tile rows of this chunk (1-D bulk copies)
+        for (int s = 0; s < total; ++s) {
+            const int st = s % PF_NT;
+            mbar_wait(&B.tempty[st], ((s / PF_NT) & 1) ^ 1, status);
+            const int pj = s / L.nkb, kb = s % L.nkb;
+            if (lane == 0) mbar_arrive_expect_tx(&B.tfull[st], 4 * TROW);
+            __syncwarp();
             if (lane < 4)
-                bulk_g2s(stage + PF_A_BYTES + PF_B_BYTES + lane * TROW,
-                         L.trellis[pj] + static_cast<size_t>(kb * 4 + lane) * L.row_stride + static_cast<size_t>(L.chunk) * TROW,
-                         TROW, &full[st]);
+                bulk_g2s(ring + PF_OFF_T + st * PF_T_BYTES + lane * TROW,
+                         (pj ? L.trellis[1] : L.trellis[0]) + static_cast<size_t>(kb * 4 + lane) * L.row_stride +
+                             static_cast<size_t>(L.chunk) * TROW,
+                         TROW, &B.tfull[st]);
+            __syncwarp();
         }
     } else if (warp == 1) {
         // MMA issuer
         constexpr uint32_t idesc = umma_idesc_f16(PF_BM, PF_BN);
         for (int s = 0; s < total; ++s) {
-            const int st = s % PF_STAGES;
-            const uint32_t ph = (s / PF_STAGES) & 1;
-            mbar_wait(&full[st], ph, status);
-            mbar_wait(&dec[st], ph, status);
+            const int sa_i = s % PF_NA, sb_i = s % PF_NB;
+            mbar_wait(&B.afull[sa_i], (s / PF_NA) & 1, status);
+            mbar_wait(&B.bfull[sb_i], (s / PF_NB) & 1, status);
             tc_fence_after();
             const int pj = s / L.nkb, kb = s % L.nkb;
             if (lane == 0) {
-                const uint32_t sa = smem_u32(ring + st * PF_STAGE);
-                const uint32_t sb = sa + PF_A_BYTES;
+                const uint32_t sa = smem_u32(ring + sa_i * PF_A_STAGE);
+                const uint32_t sb = smem_u32(ring + PF_OFF_B + sb_i * PF_B_BYTES);
+                for (int h = 0; h < L.nh; ++h)
 #pragma unroll
-                for (int k = 0; k < PF_BK / 16; ++k)
-                    umma_f16(tmem + pj * PF_BN, umma_desc_sw128(sa + k * 32), umma_desc_sw128(sb + k * 32), idesc,
-                             (kb > 0 || k > 0) ? 1u : 0u);
-                umma_commit(&empty[st]);
-                if (s == total - 1) umma_commit(accb);
+                    for (int k = 0; k < PF_BK / 16; ++k)
+                        umma_f16(tmem + (pj * PF_HALVES + h) * PF_BN, umma_desc_sw128(sa + h * PF_A_BYTES + k * 32),
+                                 umma_desc_sw128(sb + k * 32), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+                umma_commit(&B.aempty[sa_i]);
+                umma_commit(&B.bempty[sb_i]);
+                if (s == total - 1) umma_commit(&B.accb);
             }
             __syncwarp();
         }
@@ -278,28 +322,43 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, uint
         const int d = warp - 2;
         const int ktl = d >> 2, nt0 = (d & 3) * 2;
         const LaneDec ld = lane_dec<K>(lane);
-        const int n0 = lane >> 2, k0 = 2 * (lane & 3);
+        const uint32_t ring_s = smem_u32(ring);
+        // swizzled offsets of the lane's 4 words in each of its 2 tiles (fixed for the whole loop)
+        uint32_t so[2][4];
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+            const int n = (nt0 + t) * 16 + (lane >> 2);   // output column within the chunk (B row)
+            const int k = ktl * 16 + 2 * (lane & 3);      // k within the 64-wide block
+            so[t][0] = sw128_off(n, k);
+            so[t][1] = sw128_off(n + 8, k);
+            so[t][2] = sw128_off(n, k + 8);
+            so[t][3] = sw128_off(n + 8, k + 8);
+        }
+        const uint32_t tw0 = nt0 * 32 * K + ld.w0 * 4, tw1 = nt0 * 32 * K + ld.w1 * 4;
         for (int s = 0; s < total; ++s) {
-            const int st = s % PF_STAGES;
-            const uint32_t ph = (s / PF_STAGES) & 1;
-            mbar_wait(&full[st], ph, status);
-            uint8_t* stage = ring + st * PF_STAGE;
-            const uint32_t* tr = reinterpret_cast<const uint32_t*>(stage + PF_A_BYTES + PF_B_BYTES + ktl * TROW);
-            uint8_t* bt = stage + PF_A_BYTES;
+            const int st = s % PF_NT, sb_i = s % PF_NB;
+            mbar_wait(&B.tfull[st], (s / PF_NT) & 1, status);
+            const uint32_t tr = ring_s + PF_OFF_T + st * PF_T_BYTES + ktl * TROW;
+            uint32_t w[2][2];
 #pragma unroll
             for (int t = 0; t < 2; ++t) {
-                uint32_t a[4];
-                decode_afrag<K>(tr + (nt0 + t) * 8 * K, ld, a);
-                const int n = (nt0 + t) * 16 + n0;   // output column within the chunk (B row)
-                const int k = ktl * 16 + k0;          // k within the 64-wide block
-                *reinterpret_cast<uint32_t*>(bt + sw128_off(n, k)) = a[0];
-                *reinterpret_cast<uint32_t*>(bt + sw128_off(n, k + 8)) = a[2];
-                *reinterpret_cast<uint32_t*>(bt + sw128_off(n + 8, k)) = a[1];
-                *reinterpret_cast<uint32_t*>(bt + sw128_off(n + 8, k + 8)) = a[3];
+                w[t][0] = lds32(tr + t * 32 * K + tw0);
+                w[t][1] = lds32(tr + t * 32 * K + tw1);
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.tempty[st]);
+            uint32_t a[2][4];
+#pragma unroll
+            for (int t = 0; t < 2; ++t) decode_afrag_words<K>(w[t][0], w[t][1], ld.off, a[t]);
+            mbar_wait(&B.bempty[sb_i], ((s / PF_NB) & 1) ^ 1, status);
+            const uint32_t bt = ring_s + PF_OFF_B + sb_i * PF_B_BYTES;
+#pragma unroll
+            for (int t = 0; t < 2; ++t)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) sts32(bt + so[t][r], a[t][r]);
             fence_proxy_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&dec[st]);
+            if (lane == 0) mbar_arrive(&B.bfull[sb_i]);
         }
     }
 }
@@ -319,7 +378,7 @@ __device__ __forceinline__ void pf_tmem_to_smem(uint32_t tmem, int col0, float* 
 }
 
 struct PfSmem {
-    uint64_t full[PF_STAGES], dec[PF_STAGES], empty[PF_STAGES], accb;
+    PfBars bars;
     uint32_t tmem;
 };
 
@@ -332,12 +391,20 @@ __device__ __forceinline__ uint8_t* pf_ring(uint8_t* raw)
 __device__ __forceinline__ void pf_setup(PfSmem& S, int warp, int ncols)
 {
     if (threadIdx.x == 0) {
-        for (int i = 0; i < PF_STAGES; ++i) {
-            mbar_init(&S.full[i], 1);
-            mbar_init(&S.dec[i], PF_DEC);
-            mbar_init(&S.empty[i], 1);
+        PfBars& B = S.bars;
+        for (int i = 0; i < PF_NA; ++i) {
+            mbar_init(&B.afull[i], 1);
+            mbar_init(&B.aempty[i], 1);
         }
-        mbar_init(&S.accb, 1);
+        for (int i = 0; i < PF_NT; ++i) {
+            mbar_init(&B.tfull[i], 1);
+            mbar_init(&B.tempty[i], PF_DEC);
+        }
+        for (int i = 0; i < PF_NB; ++i) {
+            mbar_init(&B.bfull[i], PF_DEC);
+            mbar_init(&B.bempty[i], 1);
+        }
+        mbar_init(&B.accb, 1);
         fence_barrier_init();
     }
     if (warp == 1) {
@@ -376,7 +443,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, con
     if (chunk * 128 >= I_e) return;
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
-    pf_setup(S, warp, 256);
+    constexpr int NCOLS = 2 * PF_HALVES * PF_BN;   // (gate, up) x halves
+    pf_setup(S, warp, NCOLS);
 
     PfLoop L;
     L.amap[0] = &mg;
@@ -388,40 +456,45 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, con
     L.nproj = 2;
     L.nkb = p.H / PF_BK;
     L.row0 = t.row0;
-    if (Ke == KR) pf_mainloop<KR>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
-    else pf_mainloop<KS>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
+    L.nh = t.rows > PF_BM ? 2 : 1;
+    if (Ke == KR) pf_mainloop<KR>(L, ring, S.bars, S.tmem, warp, lane, p.status);
+    else pf_mainloop<KS>(L, ring, S.bars, S.tmem, warp, lane, p.status);
 
-    // epilogue
-    mbar_wait(&S.accb, 0, p.status);
+    // epilogue, one half at a time through the (now idle) ring
+    mbar_wait(&S.bars.accb, 0, p.status);
     tc_fence_after();
     float* G = reinterpret_cast<float*>(ring);
     float* U = G + PF_BM * PF_EPI_LD;
-    if (warp < 4) {
-        pf_tmem_to_smem(S.tmem, 0, G, warp, lane);
-        pf_tmem_to_smem(S.tmem, PF_BN, U, warp, lane);
-    }
-    __syncthreads();
     const int col = chunk * 128 + lane * 4;
     float svg[4], svu[4], sud[4];
     load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 2)) + col, svg);
     load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 5)) + col, svu);
     load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 7)) + col, sud);
     const int mode = t.shared ? p.act_shared : p.act_routed;
-    for (int r = warp; r < t.rows; r += PF_THREADS / 32) {
-        float g[4], u[4], a[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            g[i] = G[r * PF_EPI_LD + lane * 4 + i];
-            u[i] = U[r * PF_EPI_LD + lane * 4 + i];
+    for (int h = 0; h < L.nh; ++h) {
+        if (warp < 4) {
+            pf_tmem_to_smem(S.tmem, (0 * PF_HALVES + h) * PF_BN, G, warp, lane);
+            pf_tmem_to_smem(S.tmem, (1 * PF_HALVES + h) * PF_BN, U, warp, lane);
         }
-        had128_warp(g, lane);
-        had128_warp(u, lane);
+        __syncthreads();
+        const int rows_h = min(PF_BM, t.rows - h * PF_BM);
+        for (int r = warp; r < rows_h; r += PF_THREADS / 32) {
+            float g[4], u[4], a[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) a[i] = act_gated(g[i] * svg[i], u[i] * svu[i], p.limit, mode) * sud[i];
-        had128_warp(a, lane);
-        store4_half(p.ap + static_cast<size_t>(t.row0 + r) * p.imax + col, a);
+            for (int i = 0; i < 4; ++i) {
+                g[i] = G[r * PF_EPI_LD + lane * 4 + i];
+                u[i] = U[r * PF_EPI_LD + lane * 4 + i];
+            }
+            had128_warp(g, lane);
+            had128_warp(u, lane);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = act_gated(g[i] * svg[i], u[i] * svu[i], p.limit, mode) * sud[i];
+            had128_warp(a, lane);
+            store4_half(p.ap + static_cast<size_t>(t.row0 + h * PF_BM + r) * p.imax + col, a);
+        }
+        __syncthreads();
     }
-    pf_teardown(S, warp, 256);
+    pf_teardown(S, warp, NCOLS);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -439,7 +512,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_down(const PfParams p, const
     const int chunk = blockIdx.x;
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
-    pf_setup(S, warp, 128);
+    constexpr int NCOLS = PF_HALVES * PF_BN;
+    pf_setup(S, warp, NCOLS);
 
     PfLoop L;
     L.amap[0] = L.amap[1] = &ma;
@@ -449,29 +523,34 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_down(const PfParams p, const
     L.nproj = 1;
     L.nkb = I_e / PF_BK;
     L.row0 = t.row0;
-    if (Ke == KR) pf_mainloop<KR>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
-    else pf_mainloop<KS>(L, ring, S.full, S.dec, S.empty, &S.accb, S.tmem, warp, lane, p.status);
+    L.nh = t.rows > PF_BM ? 2 : 1;
+    if (Ke == KR) pf_mainloop<KR>(L, ring, S.bars, S.tmem, warp, lane, p.status);
+    else pf_mainloop<KS>(L, ring, S.bars, S.tmem, warp, lane, p.status);
 
-    mbar_wait(&S.accb, 0, p.status);
+    mbar_wait(&S.bars.accb, 0, p.status);
     tc_fence_after();
     float* D = reinterpret_cast<float*>(ring);
-    if (warp < 4) pf_tmem_to_smem(S.tmem, 0, D, warp, lane);
-    __syncthreads();
     const int col = chunk * 128 + lane * 4;
     float svd[4];
     load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 8)) + col, svd);
-    for (int r = warp; r < t.rows; r += PF_THREADS / 32) {
-        const int slot = pf_row_slot(p, t.row0 + r);
-        const float w = t.shared ? 1.0f : p.rw[slot];
-        float v[4];
+    for (int h = 0; h < L.nh; ++h) {
+        if (warp < 4) pf_tmem_to_smem(S.tmem, h * PF_BN, D, warp, lane);
+        __syncthreads();
+        const int rows_h = min(PF_BM, t.rows - h * PF_BM);
+        for (int r = warp; r < rows_h; r += PF_THREADS / 32) {
+            const int slot = pf_row_slot(p, t.row0 + h * PF_BM + r);
+            const float w = t.shared ? 1.0f : p.rw[slot];
+            float v[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = D[r * PF_EPI_LD + lane * 4 + i];
-        had128_warp(v, lane);
+            for (int i = 0; i < 4; ++i) v[i] = D[r * PF_EPI_LD + lane * 4 + i];
+            had128_warp(v, lane);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] *= svd[i] * w;
-        *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(slot) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
+            for (int i = 0; i < 4; ++i) v[i] *= svd[i] * w;
+            *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(slot) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
+        }
+        __syncthreads();
     }
-    pf_teardown(S, warp, 128);
+    pf_teardown(S, warp, NCOLS);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -621,8 +700,9 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
 
     const long long rot_items = static_cast<long long>(rows) * (p.H / 128) * 2;
     pf_rotate<<<static_cast<unsigned>((rot_items + 7) / 8), 256, 0, stream>>>(p);
-    // tile upper bound: sum over experts of ceil(n_e / 128) <= S / 128 + E, plus the shared tiles
-    const int max_tiles = (p.S_cap + PF_BM - 1) / PF_BM + p.n_local + (p.has_shared ? (p.M + PF_BM - 1) / PF_BM : 0);
+    // tile upper bound: sum over experts of ceil(n_e / T) <= S / T + E, plus the shared tiles
+    const int max_tiles = (p.S_cap + PF_TILE_ROWS - 1) / PF_TILE_ROWS + p.n_local +
+                          (p.has_shared ? (p.M + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
     const int imax_ch = L.imax / 128;
     kg<<<dim3(imax_ch, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
     kd<<<dim3(p.H / 128, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, ma);

@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     {
         const int h = tid < E ? hist[tid] : 0;
         const int r = (h + RUN_ROWS - 1) / RUN_ROWS;
-        const int mt = (h + 127) / 128;
+        const int mt = (h + PF_TILE_ROWS - 1) / PF_TILE_ROWS;
         int v0 = h, v1 = r, v2 = mt;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -454,7 +454,7 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
         for (int i = tid; i <= E; i += PERM_THREADS) a.estart[i] = estart[i];
     if (a.tstart) {
         for (int i = tid; i <= E; i += PERM_THREADS) a.tstart[i] = tsh[i];
-        if (tid == 0) a.tstart[E + 1] = tsh[E] + (a.has_shared ? (a.M + 127) / 128 : 0);
+        if (tid == 0) a.tstart[E + 1] = tsh[E] + (a.has_shared ? (a.M + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
     }
     __syncthreads();
 
