@@ -1,20 +1,23 @@
 // Prefill-shaped MoE experts on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
 // Tokens are grouped by expert (the permutation's sorted order), so each expert is a dense
-// [rows x H] x [H x I] problem. Per CTA up to 256 rows of one expert (two 128-row halves) x one
-// 128-column output chunk; both halves share every decoded weight tile:
-//   warp 0      producer: 2-D TMA loads (128B swizzle, plain per-CTA loads) of the rotated input rows
-//               of each half and 1-D bulk copies of the EXL3 trellis rows of the k-block into a
-//               4-stage ring
+// [rows x H] x [H x I] problem. A cluster of two CTAs on neighbouring SMs computes one 256-row x
+// 256-column output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16): CTA r holds
+// rows 128 r .. 128 r + 127 of the activations and decodes weight columns 128 r .. 128 r + 127,
+// the tensor cores of both SMs read both halves, and each CTA's TMEM receives its 128 rows x 256
+// columns. Per SM this reads half the shared-memory bytes per MAC of a one-SM 128 x 128 tile,
+// which is what bounds a tcgen05 kernel whose weights are written to shared memory by warps.
+//   warp 0      producer: 2-D TMA load of the CTA's activation rows (completion counted on the
+//               leader CTA's barrier) and 1-D bulk copies of its trellis rows, 6-stage ring
 //   warps 2-17  decoders: EXL3 decode of the k-block's 32 weight tiles (exact fp16, one rounding)
-//               straight into the UMMA K-major 128B-swizzled shared-memory layout
-//   warp 1      one thread issues tcgen05.mma (M=128 per half, N=128, K=16, fp16 x fp16 -> fp32 in
-//               TMEM) and commits each stage back to the producer through an mbarrier
-//   all warps   epilogue: tcgen05.ld of the accumulators, Hadamard / scales / activation in
+//               straight into the UMMA K-major 128B-swizzled layout; they arrive on the leader's
+//               barrier (the peer CTA's from across the cluster)
+//   warp 1      leader CTA: one thread issues the pair MMAs and commits each stage to both CTAs
+//   all warps   epilogue: tcgen05.ld of the CTA's accumulators, Hadamard / scales / activation in
 //               registers, fp16 or fp32 stores.
 // Kernels:
 //   pf_rotate    x -> fp16(H128(x * suh)) for gate and up, rows in expert-sorted order
-//   pf_gateup    gate and up accumulators (TMEM columns 128 (2 proj + half)), epilogue = the MoE
+//   pf_gateup    gate and up accumulators (TMEM columns 0-255 / 256-511), epilogue = the MoE
 //                coop A epilogue (exl3_moe_coop_kernel.cuh:758-808): H128, svh, SiLU*mul, suh_down,
 //                H128 -> fp16 down input
 //   pf_down      down projection, epilogue H128 * svh * routing weight -> per-slot fp32 rows
@@ -31,27 +34,22 @@
 
 namespace eva {
 
-constexpr int PF_BM = 128, PF_BN = 128, PF_BK = 64;   // PF_BM: rows of one MMA half
-constexpr int PF_HALVES = PF_TILE_ROWS / PF_BM;
+constexpr int PF_BM = 128;                               // rows per CTA: one half of the pair's M = 256
+constexpr int PF_BN = 128;                               // weight columns decoded per CTA: half of N = 256
+constexpr int PF_BK = 64;
+constexpr int PF_PAIR_N = 2 * PF_BN;
 constexpr int PF_DEC = 16;                               // decoder warps
 constexpr int NT_PF = 8;                                 // 16-column tiles per 128-column chunk
-constexpr int PF_THREADS = (3 + PF_DEC) * 32;            // A producer, MMA, 16 decoders, trellis producer
-constexpr int PF_TWARP = 2 + PF_DEC;                     // the trellis producer warp
-constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB per half
+constexpr int PF_THREADS = (2 + PF_DEC) * 32;            // producer, MMA, 16 decoders
+constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;            // 16 KB
 constexpr int PF_T_BYTES = 4 * 8 * 32 * 4;               // 4 k-tile rows x 8 tiles x 32K bytes (K <= 4)
-// three rings: activations (MMA operand A, both halves), trellis (decoder input), decoded weights
-// (MMA operand B). The trellis ring runs furthest ahead, so the decoders never wait on a TMA round
-// trip through the MMA; the decoders run up to PF_NB k-blocks ahead of the MMA.
-constexpr int PF_NA = 4, PF_NT = 8, PF_NB = 3;
-constexpr int PF_A_STAGE = PF_HALVES * PF_A_BYTES;
-constexpr int PF_OFF_B = PF_NA * PF_A_STAGE;
-constexpr int PF_OFF_T = PF_OFF_B + PF_NB * PF_B_BYTES;
-constexpr int PF_RING = PF_OFF_T + PF_NT * PF_T_BYTES;
+constexpr int PF_STAGE = PF_A_BYTES + PF_B_BYTES + PF_T_BYTES;
+constexpr int PF_STAGES = 6;
 constexpr int PF_EPI_LD = 129;                           // padded row (floats) of the epilogue tiles
-constexpr size_t PF_SMEM = 1024 + static_cast<size_t>(PF_RING) + 256;
-static_assert(PF_HALVES == 2, "two MMA halves per CTA");
-static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PF_RING, "epilogue tiles reuse the rings");
+constexpr size_t PF_SMEM = 1024 + static_cast<size_t>(PF_STAGES) * PF_STAGE + 256;
+static_assert(PF_TILE_ROWS == 2 * PF_BM, "a CTA pair covers one expert tile");
+static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PF_STAGES * PF_STAGE, "epilogue tiles reuse the ring");
 static_assert(PF_SMEM <= 227 * 1024, "shared memory per CTA");
 
 struct PfParams {
@@ -93,19 +91,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N)
     return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc)
-{
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar)
-{
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
@@ -125,13 +110,53 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar)
+// 2-D TMA load of this CTA's rows whose completion is counted on the pair leader's barrier
+// (bar: shared::cluster address). Plain per-CTA load, no cross-CTA delivery of data.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar)
 {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
             smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
         : "memory");
+}
+
+__device__ __forceinline__ void umma_f16_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t acc)
+{
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(idesc), "r"(acc));
+}
+
+// Arrive on the mbarrier at shared::cluster address bar when the pair MMAs issued so far complete.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t mapa_rank(const void* p, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -239,23 +264,24 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
 }
 
 // ---------------------------------------------------------------------------------------------
-// Shared main loop of the two GEMM kernels.
-//   nproj   projections accumulated (gate+up: 2, down: 1); accumulator (proj, half) at TMEM
-//           columns 128 (proj * 2 + half)
-//   nh      halves with rows (1 or 2)
+// Shared main loop of the two GEMM kernels (one CTA of the pair).
+//   nproj   projections accumulated (gate+up: 2, down: 1); projection j accumulates into TMEM
+//           columns 256 j .. 256 j + 255
 //   nkb     k-blocks (64) per projection
-//   amaps   tensor maps of the A rows per projection; trellis bases per projection
+//   amap    tensor maps of the activation rows per projection; trellis bases per projection
+//   chunk   the 128-column weight chunk this CTA decodes (dec_valid = 0: past the end, not decoded)
 
 struct PfLoop {
     const CUtensorMap* amap[2];
     const uint8_t* trellis[2];
     size_t row_stride;       // bytes between k-tile rows of the trellis
-    int chunk;               // 128-column output chunk
-    int nproj, nkb, row0, nh;
+    int chunk, dec_valid;
+    int nproj, nkb, row0;    // row0: this CTA's first activation row
+    uint32_t rank;           // 0 = leader (issues the MMAs)
 };
 
 struct PfBars {
-    uint64_t afull[PF_NA], aempty[PF_NA], tfull[PF_NT], tempty[PF_NT], bfull[PF_NB], bempty[PF_NB], accb;
+    uint64_t afull[PF_STAGES], tfull[PF_STAGES], bfull[PF_STAGES], empty[PF_STAGES], accb;
 };
 
 template <int K>
@@ -265,58 +291,58 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
     const int total = L.nproj * L.nkb;
     constexpr uint32_t TROW = NT_PF * 32 * K;   // bytes of one k-tile row's 8 tiles
     if (warp == 0) {
-        // activation producer: both halves' rows of the k-block (2-D TMA)
+        // producer: own activation rows (counted on the leader's afull) and own trellis rows. The
+        // MMA commits each stage to the leader's empty barrier only; the leader's producer, once it
+        // sees a stage released, forwards the release to the peer CTA's barrier.
         for (int s = 0; s < total; ++s) {
-            const int st = s % PF_NA;
-            mbar_wait(&B.aempty[st], ((s / PF_NA) & 1) ^ 1, status);
+            const int st = s % PF_STAGES;
+            mbar_wait(&B.empty[st], ((s / PF_STAGES) & 1) ^ 1, status);
+            if (L.rank == 0 && s >= PF_STAGES && lane == 0) mbar_arrive_remote(mapa_rank(&B.empty[st], 1));
             const int pj = s / L.nkb, kb = s % L.nkb;
+            uint8_t* stage = ring + st * PF_STAGE;
             if (lane == 0) {
-                uint8_t* dst = ring + st * PF_A_STAGE;
-                mbar_arrive_expect_tx(&B.afull[st], L.nh * PF_A_BYTES);
-                for (int h = 0; h < L.nh; ++h)
-                    tma_load_2d(dst + h * PF_A_BYTES, pj ? L.amap[1] : L.amap[0], kb * PF_BK, L.row0 + h * PF_BM,
-                                &B.afull[st]);
+                if (L.rank == 0) mbar_arrive_expect_tx(&B.afull[st], 2 * PF_A_BYTES);
+                tma_load_2d_pair(stage, pj ? L.amap[1] : L.amap[0], kb * PF_BK, L.row0, mapa_rank(&B.afull[st], 0));
+                if (L.dec_valid) mbar_arrive_expect_tx(&B.tfull[st], 4 * TROW);
+                else mbar_arrive(&B.tfull[st]);
             }
             __syncwarp();
-        }
-    } else if (warp == PF_TWARP) {
-        // trellis producer: the k-block's 4 k-tile rows of this chunk (1-D bulk copies)
-        for (int s = 0; s < total; ++s) {
-            const int st = s % PF_NT;
-            mbar_wait(&B.tempty[st], ((s / PF_NT) & 1) ^ 1, status);
-            const int pj = s / L.nkb, kb = s % L.nkb;
-            if (lane == 0) mbar_arrive_expect_tx(&B.tfull[st], 4 * TROW);
-            __syncwarp();
-            if (lane < 4)
-                bulk_g2s(ring + PF_OFF_T + st * PF_T_BYTES + lane * TROW,
+            if (L.dec_valid && lane < 4)
+                bulk_g2s(stage + PF_A_BYTES + PF_B_BYTES + lane * TROW,
                          (pj ? L.trellis[1] : L.trellis[0]) + static_cast<size_t>(kb * 4 + lane) * L.row_stride +
                              static_cast<size_t>(L.chunk) * TROW,
                          TROW, &B.tfull[st]);
             __syncwarp();
         }
     } else if (warp == 1) {
-        // MMA issuer
-        constexpr uint32_t idesc = umma_idesc_f16(PF_BM, PF_BN);
+        if (L.rank != 0 || lane != 0) return;
+        // leader, one thread: pair MMAs (M = 256 over both CTAs' rows, N = 256 over both CTAs'
+        // decoded columns), one commit per stage
+        constexpr uint32_t idesc = umma_idesc_f16(2 * PF_BM, PF_PAIR_N);
+        int st = 0, pj = 0, kb = 0;
+        uint32_t ph = 0;
         for (int s = 0; s < total; ++s) {
-            const int sa_i = s % PF_NA, sb_i = s % PF_NB;
-            mbar_wait(&B.afull[sa_i], (s / PF_NA) & 1, status);
-            mbar_wait(&B.bfull[sb_i], (s / PF_NB) & 1, status);
+            mbar_wait(&B.afull[st], ph, status);
+            mbar_wait(&B.bfull[st], ph, status);
             tc_fence_after();
-            const int pj = s / L.nkb, kb = s % L.nkb;
-            if (lane == 0) {
-                const uint32_t sa = smem_u32(ring + sa_i * PF_A_STAGE);
-                const uint32_t sb = smem_u32(ring + PF_OFF_B + sb_i * PF_B_BYTES);
-                for (int h = 0; h < L.nh; ++h)
+            const uint32_t sa = smem_u32(ring + st * PF_STAGE);
+            const uint32_t sb = sa + PF_A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < PF_BK / 16; ++k)
-                        umma_f16(tmem + (pj * PF_HALVES + h) * PF_BN, umma_desc_sw128(sa + h * PF_A_BYTES + k * 32),
-                                 umma_desc_sw128(sb + k * 32), idesc, (kb > 0 || k > 0) ? 1u : 0u);
-                umma_commit(&B.aempty[sa_i]);
-                umma_commit(&B.bempty[sb_i]);
-                if (s == total - 1) umma_commit(&B.accb);
+            for (int k = 0; k < PF_BK / 16; ++k)
+                umma_f16_pair(tmem + pj * PF_PAIR_N, umma_desc_sw128(sa + k * 32), umma_desc_sw128(sb + k * 32), idesc,
+                              (kb > 0 || k > 0) ? 1u : 0u);
+            umma_commit_pair(smem_u32(&B.empty[st]));
+            if (++kb == L.nkb) {
+                kb = 0;
+                ++pj;
             }
-            __syncwarp();
+            if (++st == PF_STAGES) {
+                st = 0;
+                ph ^= 1u;
+            }
         }
+        umma_commit_pair(mapa_rank(&B.accb, 0));
+        umma_commit_pair(mapa_rank(&B.accb, 1));
     } else {
         // decoders: warp d (0..15) takes k-tile row d / 4 of the block and tiles 2 (d % 4) .. +1
         const int d = warp - 2;
@@ -336,29 +362,32 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         }
         const uint32_t tw0 = nt0 * 32 * K + ld.w0 * 4, tw1 = nt0 * 32 * K + ld.w1 * 4;
         for (int s = 0; s < total; ++s) {
-            const int st = s % PF_NT, sb_i = s % PF_NB;
-            mbar_wait(&B.tfull[st], (s / PF_NT) & 1, status);
-            const uint32_t tr = ring_s + PF_OFF_T + st * PF_T_BYTES + ktl * TROW;
-            uint32_t w[2][2];
+            const int st = s % PF_STAGES;
+            mbar_wait(&B.tfull[st], (s / PF_STAGES) & 1, status);
+            if (L.dec_valid) {
+                const uint32_t stage_s = ring_s + st * PF_STAGE;
+                const uint32_t tr = stage_s + PF_A_BYTES + PF_B_BYTES + ktl * TROW;
+                const uint32_t bt = stage_s + PF_A_BYTES;
+                uint32_t w[2][2];
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-                w[t][0] = lds32(tr + t * 32 * K + tw0);
-                w[t][1] = lds32(tr + t * 32 * K + tw1);
+                for (int t = 0; t < 2; ++t) {
+                    w[t][0] = lds32(tr + t * 32 * K + tw0);
+                    w[t][1] = lds32(tr + t * 32 * K + tw1);
+                }
+#pragma unroll
+                for (int t = 0; t < 2; ++t) {
+                    uint32_t a[4];
+                    decode_afrag_words<K>(w[t][0], w[t][1], ld.off, a);
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) sts32(bt + so[t][r], a[r]);
+                }
+                fence_proxy_async_smem();
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&B.tempty[st]);
-            uint32_t a[2][4];
-#pragma unroll
-            for (int t = 0; t < 2; ++t) decode_afrag_words<K>(w[t][0], w[t][1], ld.off, a[t]);
-            mbar_wait(&B.bempty[sb_i], ((s / PF_NB) & 1) ^ 1, status);
-            const uint32_t bt = ring_s + PF_OFF_B + sb_i * PF_B_BYTES;
-#pragma unroll
-            for (int t = 0; t < 2; ++t)
-#pragma unroll
-                for (int r = 0; r < 4; ++r) sts32(bt + so[t][r], a[t][r]);
-            fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&B.bfull[sb_i]);
+            if (lane == 0) {
+                if (L.rank == 0) mbar_arrive(&B.bfull[st]);
+                else mbar_arrive_remote(mapa_rank(&B.bfull[st], 0));
+            }
         }
     }
 }
@@ -388,62 +417,60 @@ __device__ __forceinline__ uint8_t* pf_ring(uint8_t* raw)
     return raw + ((1024 - (a & 1023)) & 1023);
 }
 
+// Both CTAs of the pair: barriers, the pair's TMEM allocation (one warp per CTA, same warp), and a
+// cluster barrier so that no CTA signals the other's barriers before they exist.
 __device__ __forceinline__ void pf_setup(PfSmem& S, int warp, int ncols)
 {
     if (threadIdx.x == 0) {
         PfBars& B = S.bars;
-        for (int i = 0; i < PF_NA; ++i) {
+        for (int i = 0; i < PF_STAGES; ++i) {
             mbar_init(&B.afull[i], 1);
-            mbar_init(&B.aempty[i], 1);
-        }
-        for (int i = 0; i < PF_NT; ++i) {
             mbar_init(&B.tfull[i], 1);
-            mbar_init(&B.tempty[i], PF_DEC);
-        }
-        for (int i = 0; i < PF_NB; ++i) {
-            mbar_init(&B.bfull[i], PF_DEC);
-            mbar_init(&B.bempty[i], 1);
+            mbar_init(&B.bfull[i], 2 * PF_DEC);
+            mbar_init(&B.empty[i], 1);
         }
         mbar_init(&B.accb, 1);
         fence_barrier_init();
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem)), "r"(ncols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&S.tmem)), "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();
     tc_fence_after();
 }
 
 __device__ __forceinline__ void pf_teardown(PfSmem& S, int warp, int ncols)
 {
     tc_fence_before();
-    __syncthreads();
+    cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(S.tmem), "r"(ncols));
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(S.tmem), "r"(ncols));
     }
 }
 
 // ---------------------------------------------------------------------------------------------
-// pf_gateup: gate and up of one (expert tile, 128 columns of I)
+// pf_gateup: gate and up of one (expert tile of up to 256 rows, 256 columns of I), CTA pair
 
 template <int KR, int KS>
-__global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, const __grid_constant__ CUtensorMap mg,
-                                                          const __grid_constant__ CUtensorMap mu)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
+    pf_gateup(const PfParams p, const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mu)
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ PfSmem S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     PfTile t;
-    if (!pf_tile(p, blockIdx.y, t)) return;
+    if (!pf_tile(p, blockIdx.y, t)) return;               // both CTAs of the pair agree
     const int I_e = t.shared ? p.I_sh : p.I;
-    const int chunk = blockIdx.x;   // chunks of one row tile run next to each other: its rows stay in L2
-    if (chunk * 128 >= I_e) return;
+    const int nch = I_e / 128;
+    const int pc = blockIdx.x >> 1;
+    if (2 * pc >= nch) return;                             // both CTAs of the pair agree
+    const uint32_t rank = cluster_ctarank();
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
-    constexpr int NCOLS = 2 * PF_HALVES * PF_BN;   // (gate, up) x halves
+    constexpr int NCOLS = 2 * PF_PAIR_N;
     pf_setup(S, warp, NCOLS);
 
     PfLoop L;
@@ -452,33 +479,36 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, con
     L.trellis[0] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 0));
     L.trellis[1] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 3));
     L.row_stride = static_cast<size_t>(I_e / 16) * 32 * Ke;
-    L.chunk = chunk;
+    L.chunk = 2 * pc + static_cast<int>(rank);
+    L.dec_valid = L.chunk < nch;
     L.nproj = 2;
     L.nkb = p.H / PF_BK;
-    L.row0 = t.row0;
-    L.nh = t.rows > PF_BM ? 2 : 1;
+    L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
+    L.rank = rank;
     if (Ke == KR) pf_mainloop<KR>(L, ring, S.bars, S.tmem, warp, lane, p.status);
     else pf_mainloop<KS>(L, ring, S.bars, S.tmem, warp, lane, p.status);
 
-    // epilogue, one half at a time through the (now idle) ring
+    // epilogue: this CTA's 128 rows x the pair's 256 columns, one 128-column chunk at a time
     mbar_wait(&S.bars.accb, 0, p.status);
     tc_fence_after();
     float* G = reinterpret_cast<float*>(ring);
     float* U = G + PF_BM * PF_EPI_LD;
-    const int col = chunk * 128 + lane * 4;
-    float svg[4], svu[4], sud[4];
-    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 2)) + col, svg);
-    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 5)) + col, svu);
-    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 7)) + col, sud);
+    const int rows = min(PF_BM, t.rows - static_cast<int>(rank) * PF_BM);
     const int mode = t.shared ? p.act_shared : p.act_routed;
-    for (int h = 0; h < L.nh; ++h) {
+    for (int c = 0; c < 2; ++c) {
+        const int chunk = 2 * pc + c;
+        if (chunk >= nch) break;
         if (warp < 4) {
-            pf_tmem_to_smem(S.tmem, (0 * PF_HALVES + h) * PF_BN, G, warp, lane);
-            pf_tmem_to_smem(S.tmem, (1 * PF_HALVES + h) * PF_BN, U, warp, lane);
+            pf_tmem_to_smem(S.tmem, c * PF_BN, G, warp, lane);
+            pf_tmem_to_smem(S.tmem, PF_PAIR_N + c * PF_BN, U, warp, lane);
         }
         __syncthreads();
-        const int rows_h = min(PF_BM, t.rows - h * PF_BM);
-        for (int r = warp; r < rows_h; r += PF_THREADS / 32) {
+        const int col = chunk * 128 + lane * 4;
+        float svg[4], svu[4], sud[4];
+        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 2)) + col, svg);
+        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 5)) + col, svu);
+        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 7)) + col, sud);
+        for (int r = warp; r < rows; r += PF_THREADS / 32) {
             float g[4], u[4], a[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -490,7 +520,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, con
 #pragma unroll
             for (int i = 0; i < 4; ++i) a[i] = act_gated(g[i] * svg[i], u[i] * svu[i], p.limit, mode) * sud[i];
             had128_warp(a, lane);
-            store4_half(p.ap + static_cast<size_t>(t.row0 + h * PF_BM + r) * p.imax + col, a);
+            store4_half(p.ap + static_cast<size_t>(L.row0 + r) * p.imax + col, a);
         }
         __syncthreads();
     }
@@ -498,10 +528,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_gateup(const PfParams p, con
 }
 
 // ---------------------------------------------------------------------------------------------
-// pf_down: down projection of one (expert tile, 128 columns of H), weighted per-slot rows
+// pf_down: down projection of one (expert tile, 256 columns of H), weighted per-slot rows, CTA pair
 
 template <int KR, int KS>
-__global__ void __launch_bounds__(PF_THREADS, 1) pf_down(const PfParams p, const __grid_constant__ CUtensorMap ma)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
+    pf_down(const PfParams p, const __grid_constant__ CUtensorMap ma)
 {
     extern __shared__ uint8_t smem_raw[];
     __shared__ PfSmem S;
@@ -509,36 +540,38 @@ __global__ void __launch_bounds__(PF_THREADS, 1) pf_down(const PfParams p, const
     PfTile t;
     if (!pf_tile(p, blockIdx.y, t)) return;
     const int I_e = t.shared ? p.I_sh : p.I;
-    const int chunk = blockIdx.x;
+    const int pc = blockIdx.x >> 1;
+    const uint32_t rank = cluster_ctarank();
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
-    constexpr int NCOLS = PF_HALVES * PF_BN;
+    constexpr int NCOLS = PF_PAIR_N;
     pf_setup(S, warp, NCOLS);
 
     PfLoop L;
     L.amap[0] = L.amap[1] = &ma;
     L.trellis[0] = L.trellis[1] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 6));
     L.row_stride = static_cast<size_t>(p.H / 16) * 32 * Ke;
-    L.chunk = chunk;
+    L.chunk = 2 * pc + static_cast<int>(rank);
+    L.dec_valid = 1;                                       // H is a multiple of 256
     L.nproj = 1;
     L.nkb = I_e / PF_BK;
-    L.row0 = t.row0;
-    L.nh = t.rows > PF_BM ? 2 : 1;
+    L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
+    L.rank = rank;
     if (Ke == KR) pf_mainloop<KR>(L, ring, S.bars, S.tmem, warp, lane, p.status);
     else pf_mainloop<KS>(L, ring, S.bars, S.tmem, warp, lane, p.status);
 
     mbar_wait(&S.bars.accb, 0, p.status);
     tc_fence_after();
     float* D = reinterpret_cast<float*>(ring);
-    const int col = chunk * 128 + lane * 4;
-    float svd[4];
-    load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 8)) + col, svd);
-    for (int h = 0; h < L.nh; ++h) {
-        if (warp < 4) pf_tmem_to_smem(S.tmem, h * PF_BN, D, warp, lane);
+    const int rows = min(PF_BM, t.rows - static_cast<int>(rank) * PF_BM);
+    for (int c = 0; c < 2; ++c) {
+        if (warp < 4) pf_tmem_to_smem(S.tmem, c * PF_BN, D, warp, lane);
         __syncthreads();
-        const int rows_h = min(PF_BM, t.rows - h * PF_BM);
-        for (int r = warp; r < rows_h; r += PF_THREADS / 32) {
-            const int slot = pf_row_slot(p, t.row0 + h * PF_BM + r);
+        const int col = (2 * pc + c) * 128 + lane * 4;
+        float svd[4];
+        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 8)) + col, svd);
+        for (int r = warp; r < rows; r += PF_THREADS / 32) {
+            const int slot = pf_row_slot(p, L.row0 + r);
             const float w = t.shared ? 1.0f : p.rw[slot];
             float v[4];
 #pragma unroll
@@ -703,9 +736,9 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     // tile upper bound: sum over experts of ceil(n_e / T) <= S / T + E, plus the shared tiles
     const int max_tiles = (p.S_cap + PF_TILE_ROWS - 1) / PF_TILE_ROWS + p.n_local +
                           (p.has_shared ? (p.M + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
-    const int imax_ch = L.imax / 128;
-    kg<<<dim3(imax_ch, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
-    kd<<<dim3(p.H / 128, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, ma);
+    const int pairs_gu = (L.imax / 128 + 1) / 2;          // 256-column pairs of the widest I (odd: last pair half used)
+    kg<<<dim3(2 * pairs_gu, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
+    kd<<<dim3(2 * (p.H / 256), max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, ma);
     const long long comb = static_cast<long long>(p.M) * (p.H / 128);
     pf_combine<<<static_cast<unsigned>((comb + 7) / 8), 256, 0, stream>>>(p);
     return cudaGetLastError();
