@@ -22,7 +22,7 @@ EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_stat
            "eva_moe_arch", "eva_moe_experts_noalloc", "eva_moe_experts_decode", "eva_moe_experts_prefill",
            "eva_ep_dispatch", "eva_ep_combine", "eva_ep_arena_layout", "eva_peer_alloc", "eva_peer_open",
            "eva_peer_close", "eva_peer_free", "eva_ep_dispatch_peers", "eva_ep_wait_rows", "eva_ep_signal_partials",
-           "eva_ep_combine_peers")
+           "eva_ep_combine_peers", "eva_rmsnorm_residual")
 EP_MAX_WORLD = 32
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -106,6 +106,8 @@ def load(build_if_missing: bool = True):
         fn = getattr(L, name)
         fn.restype = ctypes.c_int
         fn.argtypes = args
+    L.eva_rmsnorm_residual.restype = ctypes.c_int
+    L.eva_rmsnorm_residual.argtypes = [i32, i32, vp, vp, vp, i32, ctypes.c_float, vp, vp]
     L.eva_moe_arch.restype = i32
     L.eva_moe_arch.argtypes = []
     _lib = L

@@ -14,7 +14,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libeva_moe.so"
-SOURCES = ["capi.cu", "routing.cu", "experts.cu", "prefill.cu", "noalloc.cu", "ep.cu"]
+SOURCES = ["capi.cu", "routing.cu", "experts.cu", "prefill.cu", "noalloc.cu", "ep.cu", "stack.cu"]
 HEADERS = ["common.cuh", "internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -90,15 +90,32 @@ class ExpertPlacement:
         return tuple(int(e) for e in np.flatnonzero(self.owner == rank))
 
 
+class _CudaView:
+    """__cuda_array_interface__ of raw device memory (a torch view of an arena region)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _device_view(ptr: int, shape, typestr: str, device) -> torch.Tensor:
+    return torch.as_tensor(_CudaView(ptr, shape, typestr), device=device)
+
+
 class CudaEpOps:
     """Device work of one rank through libeva_moe.so; no fallback."""
 
-    def __init__(self, layer: ExpertLayer, placement: ExpertPlacement, max_tokens: int, max_recv: int):
-        if not torch.cuda.is_available() or layer.device.type != "cuda":
-            raise RuntimeError("CudaEpOps requires a CUDA-resident ExpertLayer; there is no CPU fallback")
+    def __init__(self, layer: ExpertLayer, placement: ExpertPlacement, max_tokens: int, max_recv: int,
+                 residency=None):
+        device = residency.device if residency is not None else layer.device
+        if not torch.cuda.is_available() or device.type != "cuda":
+            raise RuntimeError("CudaEpOps requires a CUDA device; there is no CPU fallback")
         cfg = layer.cfg
         self.lib = _lib.load()
-        self.cfg, self.layer, self.device = cfg, layer, layer.device
+        self.cfg, self.layer, self.device = cfg, layer, device
+        self.residency = residency
+        self.router_w = layer.router_w.to(device)
+        self.router_b = layer.router_b.to(device)
         self.world = placement.world
         self.route_shape = _lib.shape_of(cfg)
         self.local_shape = _lib.shape_of(cfg, shared=False, n_experts=layer.n_local)
@@ -109,9 +126,13 @@ class CudaEpOps:
         self.owner = torch.as_tensor(placement.owner, dtype=_I32, device=self.device)
         self.local_id = torch.as_tensor(placement.local_id, dtype=_I32, device=self.device)
         self.status = torch.zeros(1, dtype=_I32, device=self.device)
-        self._tables = _lib.table_array(tuple(layer.packed.unbind(0)))
-        self._rows = tuple(layer.packed.unbind(0))
-        self._shared = _lib.shared_array(layer.shared.tolist()) if layer.shared is not None else None
+        if residency is not None:   # resident slots behind the same handle format
+            self._rows = tuple(residency.packed.unbind(0))
+            self._shared = _lib.shared_array(residency.shared_addrs)
+        else:
+            self._rows = tuple(layer.packed.unbind(0))
+            self._shared = _lib.shared_array(layer.shared.tolist()) if layer.shared is not None else None
+        self._tables = _lib.table_array(self._rows)
         self._zero_sel = torch.zeros(max_tokens, cfg.topk, dtype=_I32, device=self.device)
         self._zero_rw = torch.zeros(max_tokens, cfg.topk, dtype=_F32, device=self.device)
 
@@ -129,7 +150,7 @@ class CudaEpOps:
         idx = torch.empty(M, self.cfg.topk, dtype=_I32, device=self.device)
         w = torch.empty(M, self.cfg.topk, dtype=_F32, device=self.device)
         rc = self.lib.eva_moe_route(ctypes.byref(self.route_shape), x.data_ptr(), int(x.dtype == _BF16), M,
-                                    self.layer.router_w.data_ptr(), self.layer.router_b.data_ptr(), None,
+                                    self.router_w.data_ptr(), self.router_b.data_ptr(), None,
                                     idx.data_ptr(), w.data_ptr(), self.ws_route.data_ptr(), self.ws_route.numel(),
                                     self._stream())
         _lib.check(rc, "eva_moe_route")
@@ -208,7 +229,11 @@ class CudaEpOps:
         P.owner, P.local_id = self.owner.data_ptr(), self.local_id.data_ptr()
         self.peers = P
         self.segment_rows = segment_rows
-        self._arena_rows = world * segment_rows
+        self._arena_rows = R = world * segment_rows
+        base = own.value
+        self.recv_sel = _device_view(base + P.off_sel, (R, self.cfg.topk), "<i4", self.device)
+        self.recv_rw = _device_view(base + P.off_rw, (R, self.cfg.topk), "<f4", self.device)
+        self.part = _device_view(base + P.off_part, (R, self.cfg.hidden), "<f4", self.device)
 
     def close_peers(self, group=None):
         """Unmap the peers' arenas, then (after every rank has) free this rank's own."""
@@ -237,15 +262,46 @@ class CudaEpOps:
         _lib.check(self.lib.eva_ep_wait_rows(ctypes.byref(self.peers), self.status.data_ptr(), self._stream()),
                    "eva_ep_wait_rows")
 
-    def experts_arena(self):
-        """Routed experts of every received row, from this rank's arena into its partial rows."""
+    def _experts_call(self, rw_ptr: int, out_ptr: int):
         P = self.peers
         base = self._own_arena
         rc = self.lib.eva_moe_experts(ctypes.byref(self.local_shape), base + P.off_x, 1, self._arena_rows,
-                                      base + P.off_sel, 0, base + P.off_rw, self._tables, None,
-                                      self.ws_local.data_ptr(), self.ws_local.numel(), base + P.off_part, None,
-                                      self._stream())
+                                      base + P.off_sel, 0, rw_ptr, self._tables, None, self.ws_local.data_ptr(),
+                                      self.ws_local.numel(), out_ptr, None, self._stream())
         _lib.check(rc, "eva_moe_experts (arena)")
+
+    def experts_arena(self):
+        """Routed experts of every received row, from this rank's arena into its partial rows.
+
+        With expert residency, the experts the received rows select are made resident first (misses
+        copied from pinned host memory on the side stream); when more are selected than there are
+        slots, they run in groups that fit, each group's slots masked into its own launch and the
+        partial sums added."""
+        P = self.peers
+        base = self._own_arena
+        res = self.residency
+        if res is None:
+            self._experts_call(base + P.off_rw, base + P.off_part)
+        else:
+            active = self.recv_rw != 0
+            needed = torch.unique(self.recv_sel[active]).tolist()      # host synchronisation
+            groups = [needed[i:i + res.n_slots] for i in range(0, len(needed), res.n_slots)] or [[]]
+            if len(groups) == 1:
+                res.ensure(groups[0])
+                self._experts_call(base + P.off_rw, base + P.off_part)
+                res.mark_used()
+            else:
+                keep = torch.zeros(self.layer.n_local, dtype=torch.bool, device=self.device)
+                tmp = torch.empty_like(self.part)
+                for gi, g in enumerate(groups):
+                    res.ensure(g)
+                    keep.zero_()
+                    keep[torch.as_tensor(g, device=self.device)] = True
+                    rw_g = torch.where(keep[self.recv_sel.long()], self.recv_rw, 0.0)
+                    self._experts_call(rw_g.data_ptr(), (self.part if gi == 0 else tmp).data_ptr())
+                    res.mark_used()
+                    if gi:
+                        self.part.add_(tmp)
         _lib.check(self.lib.eva_ep_signal_partials(ctypes.byref(P), self._stream()), "eva_ep_signal_partials")
 
     def combine_peers(self, pos, base, out_bf16, out_f32=None):
@@ -270,6 +326,8 @@ class EPMoE:
     layer:      this rank's experts (layer.experts == placement.experts_of(rank)) plus the shared
                 expert and the full router
     max_tokens: most tokens one rank passes to one forward
+    residency:  optional eva_b200.residency.ExpertResidency holding this rank's experts in pinned host
+                memory with a device slot budget (then `layer` may live in host memory)
     transport:  "peers" (default with the CUDA ops: rows stored straight into the destinations' arenas
                 over NVLink by this library's kernels, segments of max_tokens rows, no host
                 synchronisation, no collective library in the step) or "nccl" (torch.distributed
@@ -279,7 +337,7 @@ class EPMoE:
     """
 
     def __init__(self, layer: ExpertLayer, placement: ExpertPlacement, *, max_tokens: int = 64,
-                 mode: str = "auto", group=None, ops=None, transport: str = "auto"):
+                 mode: str = "auto", group=None, ops=None, transport: str = "auto", residency=None):
         self.group = group
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
@@ -295,7 +353,7 @@ class EPMoE:
         self.mode = ("fixed" if max_tokens <= 64 else "exact") if mode == "auto" else mode
         self.max_recv = self.world * max_tokens
         self.capacity = self.world * max_tokens if self.mode == "fixed" else max_tokens * min(self.cfg.topk, self.world)
-        self.ops = ops if ops is not None else CudaEpOps(layer, placement, max_tokens, self.max_recv)
+        self.ops = ops if ops is not None else CudaEpOps(layer, placement, max_tokens, self.max_recv, residency)
         self.device = getattr(self.ops, "device", layer.device)
         if transport == "auto":
             transport = "peers" if isinstance(self.ops, CudaEpOps) else "nccl"
@@ -303,6 +361,8 @@ class EPMoE:
             raise ValueError("transport must be peers, nccl or auto")
         if transport == "peers" and not hasattr(self.ops, "setup_peers"):
             raise ValueError("the peers transport needs CUDA ops")
+        if getattr(self.ops, "residency", None) is not None and transport != "peers":
+            raise ValueError("expert residency runs with the peers transport")
         self.transport = transport
         if dist.is_initialized() and self.world > 1:
             dist.barrier(group)   # communicator set up before the first grouped send/recv

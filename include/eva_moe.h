@@ -247,6 +247,15 @@ int eva_ep_signal_partials(const EvaEpPeers* p, void* stream);
 int eva_ep_combine_peers(const EvaEpPeers* p, int32_t M, const int32_t* pos, const float* base, float* out_f32,
                          void* out_bf16, int32_t* status, void* stream);
 
+/* ---- layer stack ----------------------------------------------------------------------------
+ * Residual add + RMSNorm between MoE layers (runtime/ds41/model.py:968-970 `rms`, mean square in FP32,
+ * model.py:168-176): resid[m] += add[m] (add may be NULL), then
+ * h_out[m] = bf16((weight * resid[m]) * rsqrt(mean(resid[m]^2) + eps)).
+ *   resid: float [M][H] residual stream (in/out), 16-byte aligned; add: float [M][H] or NULL
+ *   weight: [H] bf16 (weight_is_bf16 = 1) or fp16; h_out: bf16 [M][H] */
+int eva_rmsnorm_residual(int32_t H, int32_t M, float* resid, const float* add, const void* weight,
+                         int32_t weight_is_bf16, float eps, void* h_out, void* stream);
+
 /* Library identification: sm arch the kernels were built for (100 for sm_100a). */
 int32_t eva_moe_arch(void);
 

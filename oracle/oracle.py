@@ -11,6 +11,7 @@ Restated from the reference (paths within Findddx/eva):
   * run table ...... runtime/ds41/moe_coop2048.py:69-111 (reference_runs / reference_table),
                      generalised to any top-k / capacity.
   * EXL3 experts ... oracle/exl3_oracle.c (C restatement, see its header).
+  * RMSNorm ........ runtime/ds41/model.py:968-970 rms(x, weight, eps) (mean square in FP32).
 
 Score functions are evaluated in float64 and rounded once to float32, so a GPU kernel that does
 the same agrees bit for bit given the same float32 logits; the reference's own float32 torch ops
@@ -278,6 +279,13 @@ def moe_forward(x_bits: np.ndarray, sel: np.ndarray, rw: np.ndarray, layer, thre
     if st:
         raise RuntimeError(f"oracle moe_forward status {st}")
     return out
+
+
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
+    """rms(x, weight, eps) = weight * x * rsqrt(mean(x^2) + eps), evaluated in float64 (float32 result)."""
+    x64 = np.asarray(x, np.float64)
+    inv = 1.0 / np.sqrt((x64 * x64).mean(axis=-1, keepdims=True) + eps)
+    return (np.asarray(w, np.float64) * x64 * inv).astype(np.float32)
 
 
 def layer_forward(x_bf16: np.ndarray, layer, threads: int = 0):

@@ -13,6 +13,8 @@ What is pinned, and by which reference function (paths within the reference proj
   swiglu.npz        runtime/ds41/kernels.py:213-217 swiglu(gate, up, limit).
   mul1.json         runtime/ds41/cpu_precision_reference.py:43-45 mul1_integer on seeded states, and
                     MUL1_SCALE.
+  rms.npz           runtime/ds41/model.py:968-970 rms(x, weight, eps) for FP32 and BF16 rows with a BF16
+                    weight.
 
 Usage: python tests/golden/make_golden.py [/path/to/reference]
 """
@@ -103,6 +105,14 @@ def main():
     (OUT / "mul1.json").write_text(json.dumps({
         "states": states, "mul1_integer": [cpr.mul1_integer(s) for s in states],
         "MUL1_SCALE": cpr.MUL1_SCALE, "MUL1_MULT": cpr.MUL1_MULT}))
+    # ---- rms (the layer-stack RMSNorm) ----------------------------------------------------------
+    torch.manual_seed(11)
+    xr = (torch.randn(6, 512) * 3).float()
+    wr = (1.0 + 0.1 * torch.randn(512)).to(torch.bfloat16)
+    out_f32 = model.rms(xr, wr, 1e-6)
+    out_bf16 = model.rms(xr.to(torch.bfloat16), wr, 1e-6)
+    np.savez_compressed(OUT / "rms.npz", x=xr.numpy(), w_bf16=wr.view(torch.int16).numpy(), eps=1e-6,
+                        out_f32=out_f32.float().numpy(), out_bf16=out_bf16.view(torch.int16).numpy())
     print("golden fixtures written to", OUT)
 
 

@@ -142,3 +142,16 @@ def test_clamp_after_differs_from_swiglu_only_above_limit(oracle):
     assert L.eo_act(12.0, 3.0, 10.0, 0) == pytest.approx(30.0)               # min(silu(12), 10) * 3
     assert L.eo_act(12.0, 3.0, 10.0, 1) == pytest.approx(10 / (1 + np.exp(-10)) * 3)
     assert L.eo_act(1.5, -20.0, 10.0, 0) == pytest.approx(L.eo_act(1.5, -20.0, 10.0, 1))
+
+
+def test_rmsnorm_matches_reference_rms(oracle):
+    """model.py:968-970 rms on FP32 and BF16 rows (tests/golden/rms.npz)."""
+    g = np.load(GOLDEN / "rms.npz")
+    w = oracle.bf16_to_f32(g["w_bf16"].view(np.uint16))
+    got = oracle.rmsnorm(g["x"], w, float(g["eps"]))
+    np.testing.assert_allclose(got, g["out_f32"], rtol=2e-6, atol=1e-6)
+    xb = oracle.f32_to_bf16(g["x"])
+    got_b = oracle.f32_to_bf16(oracle.rmsnorm(oracle.bf16_to_f32(xb), w, float(g["eps"])))
+    ref_b = g["out_bf16"].view(np.uint16)
+    diff = np.abs(got_b.astype(np.int32) - ref_b.astype(np.int32))
+    assert diff.max() <= 1 and (diff == 0).mean() > 0.99
