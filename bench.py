@@ -56,6 +56,12 @@ def parse():
     ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--prefill-only", action="store_true")
+    ap.add_argument("--stack", action="store_true",
+                    help="config 5: decode stream through --stack-layers MoE layers (RMSNorm + residual, "
+                         "attention stubbed), expert parallel over the ranks")
+    ap.add_argument("--stack-layers", type=int, default=58)
+    ap.add_argument("--residency", type=float, default=1.0,
+                    help="--stack: fraction of each rank's experts resident on the device (misses from pinned host)")
     ap.add_argument("--ep-transport", default="peers", choices=["peers", "nccl"],
                     help="N > 1: rows exchanged through NVLink peer memory by this library's kernels, or NCCL")
     return ap.parse_args()
@@ -455,6 +461,105 @@ def ep_bench(args, cfg, dev, rank, world, local):
     dist.destroy_process_group()
 
 
+def stack_bench(args, cfg, dev, rank, world, local):
+    """Config 5: a decode stream of batch --batch per rank through --stack-layers layers, experts
+    sharded over the ranks (EPMoE, peer-memory exchange), optionally only --residency of each rank's
+    experts resident (ExpertResidency: misses copied from pinned host memory on a side stream)."""
+    import math
+    import torch
+    import torch.distributed as dist
+    from eva_b200.ep import EPMoE, ExpertPlacement
+    from eva_b200.experts import make_layer
+    from eva_b200.residency import ExpertResidency
+    from eva_b200.stack import MoEStack, make_norms
+
+    L, M = args.stack_layers, args.batch
+    pl = ExpertPlacement.balanced(zipf_load(cfg), world)
+    mine = pl.experts_of(rank)
+    n_slots = max(1, math.ceil(args.residency * len(mine)))
+    if args.residency < 1.0:
+        # every rank pins its experts of every layer in host memory: refuse rather than exhaust it
+        rec = 3 * cfg.hidden * cfg.inter * cfg.bits // 8 + 6 * (cfg.hidden + cfg.inter)
+        need = L * len(mine) * (rec + 4096) * int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+        if need > 0.7 * avail:
+            raise SystemExit(f"--residency {args.residency}: {need / 2**30:.0f} GiB of pinned host memory over the "
+                             f"node's ranks, {avail / 2**30:.0f} GiB available; use fewer --stack-layers")
+    layers, residencies = [], []
+    t_build = time.perf_counter()
+    for li in range(L):
+        lay = make_layer(cfg, dev, seed=1000 + li, experts=mine)
+        lay = dataclasses_replace(lay, router_b=zipf_bias(cfg, lay.router_b))
+        if args.residency < 1.0:
+            host = lay.host_copy()
+            del lay
+            res = ExpertResidency(host, n_slots, dev)
+            residencies.append(res)
+            layers.append(EPMoE(host, pl, max_tokens=M, residency=res))
+        else:
+            layers.append(EPMoE(lay, pl, max_tokens=M))
+    norms = make_norms(L, cfg.hidden, dev, seed=5)
+    stack = MoEStack(layers, norms)
+    t_build = time.perf_counter() - t_build
+    steps, warmup = args.steps, max(3, args.warmup)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    xs = torch.randn(steps + warmup, M, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    for i in range(warmup):
+        stack.forward(xs[i], out=out)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    for r in residencies:
+        r.stats.update(hits=0, misses=0, h2d_bytes=0)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    t0.record()
+    for i in range(steps):
+        stack.forward(xs[warmup + i], out=out)
+    t1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - w0
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        ms = _max_over_ranks(ms, dev)
+    st = 0
+    for lay in layers:
+        st |= lay.status()
+    h2d = sum(r.stats["h2d_bytes"] for r in residencies)
+    misses = sum(r.stats["misses"] for r in residencies)
+    hits = sum(r.stats["hits"] for r in residencies)
+    if world > 1:
+        st = int(_max_over_ranks(st, dev))
+        h2d = _max_over_ranks(h2d, dev)
+    line = {"metric": "moe_stack_decode_tokens_per_s", "value": M * world * steps / (ms * 1e-3), "unit": UNIT,
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (EXL3 K3), bf16 in/out, fp32 residual",
+            "data": "synthetic (seeded random EXL3 trellis codes; Zipf-skewed router bias)",
+            "config": {"workload": f"config 5: {L} DeepSeek-{cfg.name.upper()} MoE layers, RMSNorm + residual, "
+                                   f"attention stubbed, decode batch {M} tokens/step per GPU, expert parallel over "
+                                   f"{world} GPUs", "layers": L, "batch": M, "global_batch": M * world,
+                       "experts_per_gpu_per_layer": len(mine), "residency": args.residency,
+                       "device_slots_per_layer": n_slots if residencies else len(mine),
+                       "parallelism": f"ep{world}", "exchange": EXCHANGE["peers"]},
+            "residency_stats": {"h2d_bytes_per_step_max_rank": h2d / steps, "misses": misses, "hits": hits}
+                               if residencies else None,
+            "wall_ms_per_step": 1e3 * wall / steps, "build_s": t_build, "device_status": st}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    for lay in layers:
+        lay.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def dataclasses_replace(obj, **kw):
+    import dataclasses
+    return dataclasses.replace(obj, **kw)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -479,6 +584,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.small:
         cfg = cfg.with_(n_experts=64, n_group=8, topk_group=4)
+    if args.stack:
+        return stack_bench(args, cfg, dev, rank, world, local)
     if world > 1:
         return ep_bench(args, cfg, dev, rank, world, local)
     if args.prefill_only:
