@@ -87,21 +87,30 @@ int num_sms()
     return cached[dev];
 }
 
+// Shape of an experts / permutation call: the slots per row (topk) may exceed the experts in the tables
+// (an expert-parallel shard holds n_experts / world of them; the other slots are inactive).
 static bool shape_ok(const EvaMoeShape* s)
 {
     if (!s) return false;
     if (s->hidden <= 0 || s->hidden % 256) return false;
     if (s->inter <= 0 || s->inter % 128) return false;
     if (s->n_experts < 1 || s->n_experts > 1024) return false;
-    if (s->topk < 1 || s->topk > 32 || s->topk > s->n_experts) return false;
+    if (s->topk < 1 || s->topk > 32) return false;
     if (s->bits < 2 || s->bits > 4) return false;
     if (s->shared_inter < 0 || s->shared_inter % 128) return false;
     if (s->shared_inter && (s->shared_bits < 2 || s->shared_bits > 4)) return false;
+    if (s->act_routed < 0 || s->act_routed > 1 || s->act_shared < 0 || s->act_shared > 1) return false;
+    return true;
+}
+
+// Shape of a routing call: top-k over all n_experts, group limits consistent.
+static bool route_ok(const EvaMoeShape* s)
+{
+    if (!shape_ok(s) || s->topk > s->n_experts) return false;
     if (s->router < 0 || s->router > 2) return false;
     if (s->n_group < 1 || s->n_group > 32 || s->n_experts % s->n_group) return false;
     if (s->topk_group < 1 || s->topk_group > s->n_group) return false;
     if (s->n_group > 1 && s->topk > s->topk_group * (s->n_experts / s->n_group)) return false;
-    if (s->act_routed < 0 || s->act_routed > 1 || s->act_shared < 0 || s->act_shared > 1) return false;
     return true;
 }
 
@@ -154,7 +163,7 @@ int eva_moe_read_status(const void* workspace, int32_t* status_host, void* strea
 int eva_moe_topk(const EvaMoeShape* shape, const float* logits, int32_t M, const float* router_b,
                  int32_t* idx_out, float* w_out, void* stream)
 {
-    if (!shape_ok(shape) || M < 0 || !logits || !idx_out || !w_out) return EVA_ERR_INVALID;
+    if (!route_ok(shape) || M < 0 || !logits || !idx_out || !w_out) return EVA_ERR_INVALID;
     if (M == 0) return EVA_OK;
     return cuda_status(launch_topk(*shape, logits, 1, M, router_b, nullptr, idx_out, w_out, static_cast<cudaStream_t>(stream)));
 }
@@ -163,7 +172,7 @@ int eva_moe_route(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, in
                   const float* router_b, float* logits_out, int32_t* idx_out, float* w_out, void* workspace,
                   size_t workspace_bytes, void* stream)
 {
-    if (!shape_ok(shape) || M < 0 || !x || !router_w || !idx_out || !w_out || !workspace) return EVA_ERR_INVALID;
+    if (!route_ok(shape) || M < 0 || !x || !router_w || !idx_out || !w_out || !workspace) return EVA_ERR_INVALID;
     if (!aligned(x, 8) || !aligned(router_w, 16)) return EVA_ERR_INVALID;
     if (M == 0) return EVA_OK;
     const WsLayout L = ws_layout(*shape, M);
@@ -280,7 +289,7 @@ int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, 
                     size_t workspace_bytes, float* out_f32, void* out_bf16, float* logits_out, int32_t* idx_out,
                     float* w_out, void* stream)
 {
-    if (!shape_ok(shape) || M < 0 || !workspace) return EVA_ERR_INVALID;
+    if (!route_ok(shape) || M < 0 || !workspace) return EVA_ERR_INVALID;
     if (M == 0) return EVA_OK;
     const WsLayout L = ws_layout(*shape, M);
     if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
