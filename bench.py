@@ -292,6 +292,37 @@ def zipf_load(cfg, seed=3):
     return rank ** -ZIPF_S
 
 
+def measured_load(cfg, dev, rank, M, seed=0):
+    """Expected cost per expert for placement, from routing a calibration batch of the prefill shape
+    (every rank routes its own, counts summed over ranks): a tensor-core tile of 256 rows decodes the
+    expert's whole weight slice, so cost = tiles + rows / 4096."""
+    import ctypes
+    import torch
+    import torch.distributed as dist
+    from eva_b200 import _lib
+    from eva_b200.experts import make_router
+    lib = _lib.load()
+    w, b = make_router(cfg, dev, seed)
+    b = zipf_bias(cfg, b)
+    shape = _lib.shape_of(cfg)
+    ws = torch.zeros(lib.eva_moe_workspace_bytes(ctypes.byref(shape), M), dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(101 + rank)          # a calibration batch, not the timed inputs
+    x = torch.randn(M, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+    idx = torch.empty(M, cfg.topk, dtype=torch.int32, device=dev)
+    wt = torch.empty(M, cfg.topk, device=dev)
+    _lib.check(lib.eva_moe_route(ctypes.byref(shape), x.data_ptr(), 1, M, w.data_ptr(), b.data_ptr(), None,
+                                 idx.data_ptr(), wt.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 torch.cuda.current_stream(dev).cuda_stream), "route")
+    rows = torch.bincount(idx.view(-1).long(), minlength=cfg.n_experts).to(torch.float64)
+    if dist.is_initialized():
+        dist.all_reduce(rows)
+    rows = rows.cpu().numpy()
+    del ws
+    torch.cuda.empty_cache()
+    return -(-rows // 256) + rows / 4096.0
+
+
 def _max_over_ranks(v, dev):
     import torch
     import torch.distributed as dist
@@ -311,7 +342,7 @@ def ep_bench(args, cfg, dev, rank, world, local):
     from eva_b200.ep import EPMoE, ExpertPlacement
     from eva_b200.experts import make_layer
 
-    pl = ExpertPlacement.balanced(zipf_load(cfg), world)
+    pl = ExpertPlacement.balanced(measured_load(cfg, dev, rank, args.prefill_tokens), world)
     layer = make_layer(cfg, dev, seed=0, experts=pl.experts_of(rank))
     owner = torch.as_tensor(pl.owner, dtype=torch.int64)
     M = args.batch
@@ -441,7 +472,7 @@ def ep_bench(args, cfg, dev, rank, world, local):
                    "tokens_per_step": P * world, "tokens_per_gpu": P, "ms_per_step": pms, "steps": psteps,
                    "parallelism": f"ep{world}", "device_status": pst,
                    "routing": f"router bias + {ZIPF_BETA} * log(rank^-{ZIPF_S}) (Zipf-skewed); experts placed on "
-                              f"ranks by expected load",
+                              f"ranks by the routed load of a calibration batch (tiles + rows/4096 per expert)",
                    "exchange": EXCHANGE[args.ep_transport] if args.ep_transport == "peers" else
                                "exact splits (counts all-to-all + one host sync), grouped NCCL send/recv of rows, "
                                "all-to-all of FP32 partial sums back",

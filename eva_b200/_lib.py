@@ -22,7 +22,7 @@ EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_stat
            "eva_moe_arch", "eva_moe_experts_noalloc", "eva_moe_experts_decode", "eva_moe_experts_prefill",
            "eva_ep_dispatch", "eva_ep_combine", "eva_ep_arena_layout", "eva_peer_alloc", "eva_peer_open",
            "eva_peer_close", "eva_peer_free", "eva_ep_dispatch_peers", "eva_ep_wait_rows", "eva_ep_signal_partials",
-           "eva_ep_combine_peers", "eva_rmsnorm_residual")
+           "eva_ep_combine_peers", "eva_rmsnorm_residual", "eva_moe_experts_window")
 EP_MAX_WORLD = 32
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -100,12 +100,15 @@ def load(build_if_missing: bool = True):
     pp = P(EvaEpPeers)
     for name, args in (("eva_ep_arena_layout", [pp]), ("eva_peer_alloc", [sz, P(vp), vp]), ("eva_peer_open", [vp, P(vp)]),
                        ("eva_peer_close", [vp]), ("eva_peer_free", [vp]),
-                       ("eva_ep_dispatch_peers", [pp, vp, i32, vp, vp, vp, vp, vp, vp]),
+                       ("eva_ep_dispatch_peers", [pp, vp, i32, vp, vp, i32, vp, vp, vp, vp]),
                        ("eva_ep_wait_rows", [pp, vp, vp]), ("eva_ep_signal_partials", [pp, vp]),
                        ("eva_ep_combine_peers", [pp, i32, vp, vp, vp, vp, vp, vp])):
         fn = getattr(L, name)
         fn.restype = ctypes.c_int
         fn.argtypes = args
+    L.eva_moe_experts_window.restype = ctypes.c_int
+    L.eva_moe_experts_window.argtypes = [shp, vp, i32, i32, vp, i32, vp, P(vp), P(ctypes.c_int64), i32, i32, vp, sz,
+                                         vp, vp, vp]
     L.eva_rmsnorm_residual.restype = ctypes.c_int
     L.eva_rmsnorm_residual.argtypes = [i32, i32, vp, vp, vp, i32, ctypes.c_float, vp, vp]
     L.eva_moe_arch.restype = i32

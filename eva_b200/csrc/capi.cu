@@ -131,6 +131,8 @@ static void fill_permute(PermuteArgs& pa, const EvaMoeShape& s, const void* sel,
     pa.capacity = capacity;
     pa.has_shared = s.shared_inter > 0;
     pa.H = s.hidden;
+    pa.sh0 = 0;
+    pa.shn = pa.has_shared ? M : 0;
 }
 
 }  // namespace eva
@@ -204,8 +206,13 @@ namespace eva {
 int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
                  int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
                  void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,
-                 bool allow_split, int path)
+                 bool allow_split, int path, int shared_row0, int shared_rows)
 {
+    if (shared_rows < 0) {
+        shared_row0 = 0;
+        shared_rows = M;
+    }
+    if (shared_row0 < 0 || shared_row0 + shared_rows > M) return EVA_ERR_INVALID;
     if (!shape_ok(shape) || M < 0 || !x || !sel || !rw || !tables || !workspace) return EVA_ERR_INVALID;
     if (!out_f32 && !out_bf16) return EVA_ERR_INVALID;
     if (shape->shared_inter && !shared) return EVA_ERR_INVALID;
@@ -233,6 +240,8 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
     pa.status = reinterpret_cast<int32_t*>(ws + L.status);
     pa.out_f32 = out_f32;
     pa.out_bf16 = out_bf16;
+    pa.sh0 = shared_row0;
+    pa.shn = shape->shared_inter ? shared_rows : 0;
     cudaError_t e = launch_permute(pa, st);
     if (e != cudaSuccess) return EVA_ERR_CUDA;
     ExpertsArgs ea;
@@ -252,6 +261,8 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
     ea.L = L;
     ea.out_f32 = out_f32;
     ea.out_bf16 = out_bf16;
+    ea.sh0 = shared_row0;
+    ea.shn = shape->shared_inter ? shared_rows : 0;
     const bool tensor = path == 2 || (path == 0 && M >= PREFILL_MIN_ROWS);
     return cuda_status(tensor ? launch_prefill(ea, st) : launch_experts(ea, st));
 }
@@ -274,6 +285,16 @@ int eva_moe_experts_prefill(const EvaMoeShape* shape, const void* x, int32_t x_i
 {
     return experts_impl(shape, x, x_is_bf16, M, sel, sel_is_i64, rw, tables, shared, workspace, workspace_bytes,
                         out_f32, out_bf16, static_cast<cudaStream_t>(stream), true, 2);
+}
+
+int eva_moe_experts_window(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
+                           int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
+                           int32_t shared_row0, int32_t shared_rows, void* workspace, size_t workspace_bytes,
+                           float* out_f32, void* out_bf16, void* stream)
+{
+    if (shared_rows < 0) return EVA_ERR_INVALID;
+    return experts_impl(shape, x, x_is_bf16, M, sel, sel_is_i64, rw, tables, shared, workspace, workspace_bytes,
+                        out_f32, out_bf16, static_cast<cudaStream_t>(stream), true, 0, shared_row0, shared_rows);
 }
 
 int eva_moe_experts_decode(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,

@@ -41,6 +41,7 @@ struct EpDispatchArgs {
     float* send_rw;
     int32_t* status;
     uint32_t* epoch;         // peer-memory exchange: this rank's step counter, advanced by the plan
+    int force_self;          // >= 0: every token also goes to this rank
 };
 
 __device__ __forceinline__ int slot_dest(const EpDispatchArgs& a, int m, int j, bool flag)
@@ -73,11 +74,13 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) ep_plan_kernel(EpDispatchArgs
     for (int c0 = 0; c0 < a.M; c0 += EP_PLAN_THREADS) {
         const int m = c0 + tid;
         uint32_t mask = 0;
-        if (m < a.M)
+        if (m < a.M) {
             for (int j = 0; j < a.topk; ++j) {
                 const int r = slot_dest(a, m, j, true);
                 if (r >= 0) mask |= 1u << r;
             }
+            if (a.force_self >= 0) mask |= 1u << a.force_self;
+        }
         for (int r = 0; r < a.world; ++r) {
             const bool bit = (mask >> r) & 1u;
             const uint32_t b = __ballot_sync(0xffffffffu, bit);
@@ -217,7 +220,7 @@ extern "C" int eva_ep_dispatch(int32_t H, int32_t topk, int32_t n_experts, const
     if (!al16(x) || !al16(send_x)) return EVA_ERR_INVALID;
     EpDispatchArgs a{H, topk, n_experts, M, world, capacity, segment_rows, x_elem_bytes, 0,
                      static_cast<const uint8_t*>(x), idx, w, owner, local_id, counts, pos,
-                     static_cast<uint8_t*>(send_x), send_sel, send_rw, status, nullptr};
+                     static_cast<uint8_t*>(send_x), send_sel, send_rw, status, nullptr, -1};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     ep_plan_kernel<<<1, EP_PLAN_THREADS, 0, s>>>(a);
     const long long warps = static_cast<long long>(M) * world + (segment_rows > 0 ? static_cast<long long>(world) * segment_rows : 0);
@@ -455,7 +458,8 @@ extern "C" int eva_peer_free(void* ptr)
 }
 
 extern "C" int eva_ep_dispatch_peers(const EvaEpPeers* p, const void* x, int32_t M, const int32_t* idx,
-                                     const float* w, int32_t* counts, int32_t* pos, int32_t* status, void* stream)
+                                     const float* w, int32_t all_to_self, int32_t* counts, int32_t* pos,
+                                     int32_t* status, void* stream)
 {
     if (!peers_ok(p) || M < 0 || !counts || (M > 0 && (!x || !idx || !w || !pos)) || !p->owner || !p->local_id)
         return EVA_ERR_INVALID;
@@ -463,7 +467,8 @@ extern "C" int eva_ep_dispatch_peers(const EvaEpPeers* p, const void* x, int32_t
     EpDispatchArgs a{p->H, p->topk, p->n_experts, M, p->world, p->world * p->segment_rows, p->segment_rows,
                      p->x_elem_bytes, 1, static_cast<const uint8_t*>(x), idx, w, p->owner, p->local_id, counts, pos,
                      nullptr, nullptr, nullptr, status,
-                     reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(p->arena[p->rank]) + FLAG_EPOCH)};
+                     reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(p->arena[p->rank]) + FLAG_EPOCH),
+                     all_to_self ? p->rank : -1};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     ep_plan_kernel<<<1, EP_PLAN_THREADS, 0, s>>>(a);
     const long long warps = static_cast<long long>(M) * p->world + static_cast<long long>(p->world) * p->segment_rows;

@@ -44,6 +44,7 @@ constexpr size_t SMEM_BYTES = static_cast<size_t>(NSTAGE) * STAGE_BYTES + RED_FL
 struct KParams {
     // shape
     int M, H, I, topk, n_local, K, I_sh, K_sh, has_shared, S_cap, imax, split_a, hpad, ipad;
+    int sh0, shn;   // the shared expert's tokens: sh0 .. sh0 + shn - 1
     int act_routed, act_shared;
     float limit;
     // inputs
@@ -88,7 +89,7 @@ struct Geo {
 };
 
 __device__ __forceinline__ int n_runs_routed(const KParams& p) { return p.runs[0]; }
-__device__ __forceinline__ int n_runs_shared(const KParams& p) { return p.has_shared ? (p.M + RUN_ROWS - 1) / RUN_ROWS : 0; }
+__device__ __forceinline__ int n_runs_shared(const KParams& p) { return p.has_shared ? (p.shn + RUN_ROWS - 1) / RUN_ROWS : 0; }
 
 __device__ __forceinline__ RunInfo run_info(const KParams& p, int r)
 {
@@ -103,7 +104,7 @@ __device__ __forceinline__ RunInfo run_info(const KParams& p, int r)
     } else {
         ri.shared = true;
         const int j = r - nr;
-        ri.nrows = min(RUN_ROWS, p.M - j * RUN_ROWS);
+        ri.nrows = min(RUN_ROWS, p.shn - j * RUN_ROWS);
         ri.expert = -1;
         ri.I = p.I_sh;
         ri.K = p.K_sh;
@@ -116,7 +117,7 @@ __device__ __forceinline__ int run_slot(const KParams& p, int r, int t)
 {
     const int nr = n_runs_routed(p);
     if (r < nr) return p.runs[2 + p.S_cap + 1 + p.runs[2 + r] + t];
-    return p.S_cap + (r - nr) * RUN_ROWS + t;
+    return p.S_cap + p.sh0 + (r - nr) * RUN_ROWS + t;
 }
 
 __device__ __forceinline__ int slot_token(const KParams& p, int s) { return s < p.S_cap ? s / p.topk : s - p.S_cap; }
@@ -634,7 +635,7 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                     o[2] += d.z;
                     o[3] += d.w;
                 }
-                if (p.has_shared) {
+                if (p.has_shared && tok >= p.sh0 && tok < p.sh0 + p.shn) {
                     const float4 d = __ldcg(reinterpret_cast<const float4*>(
                         p.dpart + (static_cast<size_t>(p.S_cap) + tok) * p.H + col));
                     o[0] += d.x;
@@ -686,6 +687,8 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
     p.I_sh = s.shared_inter;
     p.K_sh = s.shared_inter ? s.shared_bits : s.bits;
     p.has_shared = s.shared_inter > 0;
+    p.sh0 = a.sh0;
+    p.shn = p.has_shared ? a.shn : 0;
     p.S_cap = a.M * s.topk;
     p.imax = L.imax;
     p.hpad = L.hpad;
@@ -721,7 +724,7 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
 
     // split the gate/up k range when there are too few gate/up items to fill the GPU
     const int sms = num_sms();
-    const int r_max = a.M * s.topk + (p.has_shared ? (a.M + RUN_ROWS - 1) / RUN_ROWS : 0);
+    const int r_max = a.M * s.topk + (p.has_shared ? (p.shn + RUN_ROWS - 1) / RUN_ROWS : 0);
     const int items_a = r_max * (L.imax / 128);
     int split = 1;
     // a split boundary must fall on a 128 chunk of the input (per-chunk input sums)

@@ -42,6 +42,7 @@ struct PermuteArgs {
     int sel64;
     const float* rw;
     int M, topk, n_local, capacity, has_shared, H;
+    int sh0, shn;               // the shared expert applies to tokens sh0 .. sh0 + shn - 1
     const int64_t* tables[9];   // may be null: no pointer validation
     int32_t* runs;
     int32_t* run_expert;        // may be null
@@ -70,6 +71,7 @@ struct ExpertsArgs {
     WsLayout L;
     float* out_f32;
     void* out_bf16;
+    int sh0, shn;               // shared-expert token window
 };
 cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream);
 cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream);
@@ -81,7 +83,8 @@ constexpr int PF_TILE_ROWS = 256;       // rows of one expert per tensor-core CT
 int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
                  int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
                  void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,
-                 bool allow_split = true, int path = 0);   // path: 0 by size, 1 decode kernel, 2 tensor-core
+                 bool allow_split = true, int path = 0,     // path: 0 by size, 1 decode kernel, 2 tensor-core
+                 int shared_row0 = 0, int shared_rows = -1); // shared expert on rows row0 .. row0 + rows - 1 (-1: all)
 
 cudaError_t launch_dequant(const void* trellis, int in, int out, int K, uint16_t* w, cudaStream_t stream);
 

@@ -54,6 +54,7 @@ static_assert(PF_SMEM <= 227 * 1024, "shared memory per CTA");
 
 struct PfParams {
     int M, H, I, I_sh, topk, S_cap, n_local, K, K_sh, has_shared, imax, act_routed, act_shared;
+    int sh0, shn;           // the shared expert's tokens: sh0 .. sh0 + shn - 1
     float limit;
     const void* x;
     int x_bf16;
@@ -199,8 +200,8 @@ __device__ __forceinline__ bool pf_tile(const PfParams& p, int mt, PfTile& t)
         t.e = E;
         t.shared = true;
         const int j = mt - p.tstart[E];
-        t.row0 = p.S_cap + j * PF_TILE_ROWS;
-        t.rows = min(PF_TILE_ROWS, p.M - j * PF_TILE_ROWS);
+        t.row0 = p.S_cap + p.sh0 + j * PF_TILE_ROWS;
+        t.rows = min(PF_TILE_ROWS, p.shn - j * PF_TILE_ROWS);
         return true;
     }
     int lo = 0, hi = E - 1;   // last e with tstart[e] <= mt
@@ -243,8 +244,8 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
     int tok;
     const __half* suh;
     if (pos >= p.S_cap) {
-        if (!p.has_shared) return;
         tok = pos - p.S_cap;
+        if (!p.has_shared || tok < p.sh0 || tok >= p.sh0 + p.shn) return;
         suh = reinterpret_cast<const __half*>(p.sh[pj ? 4 : 1]);
     } else {
         if (pos >= p.runs[2 + p.runs[0]]) return;   // past the active rows
@@ -607,7 +608,7 @@ __global__ void __launch_bounds__(256) pf_combine(const PfParams p)
         o[2] += d.z;
         o[3] += d.w;
     }
-    if (p.has_shared) {
+    if (p.has_shared && tok >= p.sh0 && tok < p.sh0 + p.shn) {
         const float4 d = *reinterpret_cast<const float4*>(p.dpart + (static_cast<size_t>(p.S_cap) + tok) * p.H + col);
         o[0] += d.x;
         o[1] += d.y;
@@ -685,6 +686,8 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     p.K = s.bits;
     p.K_sh = s.shared_inter ? s.shared_bits : s.bits;
     p.has_shared = s.shared_inter > 0;
+    p.sh0 = a.sh0;
+    p.shn = p.has_shared ? a.shn : 0;
     p.imax = L.imax;
     p.act_routed = s.act_routed;
     p.act_shared = s.act_shared;
@@ -735,7 +738,7 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     pf_rotate<<<static_cast<unsigned>((rot_items + 7) / 8), 256, 0, stream>>>(p);
     // tile upper bound: sum over experts of ceil(n_e / T) <= S / T + E, plus the shared tiles
     const int max_tiles = (p.S_cap + PF_TILE_ROWS - 1) / PF_TILE_ROWS + p.n_local +
-                          (p.has_shared ? (p.M + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
+                          (p.has_shared ? (p.shn + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
     const int pairs_gu = (L.imax / 128 + 1) / 2;          // 256-column pairs of the widest I (odd: last pair half used)
     kg<<<dim3(2 * pairs_gu, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
     kd<<<dim3(2 * (p.H / 256), max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, ma);

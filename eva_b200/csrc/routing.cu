@@ -454,18 +454,18 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
         for (int i = tid; i <= E; i += PERM_THREADS) a.estart[i] = estart[i];
     if (a.tstart) {
         for (int i = tid; i <= E; i += PERM_THREADS) a.tstart[i] = tsh[i];
-        if (tid == 0) a.tstart[E + 1] = tsh[E] + (a.has_shared ? (a.M + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
+        if (tid == 0) a.tstart[E + 1] = tsh[E] + (a.has_shared ? (a.shn + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
     }
     __syncthreads();
 
     // 5. expected combine arrivals; rows nobody will write are zeroed here
     if (a.tok_expect) {
         for (int m = tid; m < a.M; m += PERM_THREADS) {
-            const int n = a.tok_expect[m] + (a.has_shared ? 1 : 0);
-            a.tok_expect[m] = n;
+            const bool sh = a.has_shared && m >= a.sh0 && m < a.sh0 + a.shn;
+            a.tok_expect[m] += sh ? 1 : 0;
         }
         __syncthreads();
-        if (!a.has_shared) {
+        {
             // warp per row; only rows without arrivals are written (H is a multiple of 256)
             for (int m = warp; m < a.M; m += PERM_THREADS / 32) {
                 if (a.tok_expect[m] != 0) continue;

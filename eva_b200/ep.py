@@ -13,7 +13,8 @@ One forward on every rank (all ranks call it together, each with its own tokens)
      there, each row once, with the slots of other ranks' experts given weight 0
   3. exchange row counts (exact mode only; one host synchronisation) and the rows themselves
      (one grouped send/recv of x rows, expert ids and weights)
-  4. shared expert on its own tokens (overlaps the exchange), routed experts on the received rows
+  4. routed experts on the received rows, with the shared expert of its own tokens (sent to itself,
+     all of them, as one segment) in the same launch (the NCCL transport runs it separately)
   5. return the weighted partial sums to the tokens' ranks (all-to-all) and add them up in rank
      order on top of the shared output
 
@@ -121,7 +122,8 @@ class CudaEpOps:
         self.local_shape = _lib.shape_of(cfg, shared=False, n_experts=layer.n_local)
         self.shared_shape = _lib.shape_of(cfg, n_experts=layer.n_local)
         self.ws_route = self._ws(self.route_shape, max_tokens)
-        self.ws_local = self._ws(self.local_shape, max_recv)
+        # the arena launch runs the own tokens' shared expert too: size for the shared shape
+        self.ws_local = self._ws(self.shared_shape if layer.shared is not None else self.local_shape, max_recv)
         self.ws_shared = self._ws(self.shared_shape, max_tokens) if layer.shared is not None else None
         self.owner = torch.as_tensor(placement.owner, dtype=_I32, device=self.device)
         self.local_id = torch.as_tensor(placement.local_id, dtype=_I32, device=self.device)
@@ -135,6 +137,10 @@ class CudaEpOps:
         self._tables = _lib.table_array(self._rows)
         self._zero_sel = torch.zeros(max_tokens, cfg.topk, dtype=_I32, device=self.device)
         self._zero_rw = torch.zeros(max_tokens, cfg.topk, dtype=_F32, device=self.device)
+
+    @property
+    def has_shared(self) -> bool:
+        return self._shared is not None
 
     def _ws(self, shape, rows):
         n = self.lib.eva_moe_workspace_bytes(ctypes.byref(shape), max(rows, 1))
@@ -249,12 +255,13 @@ class CudaEpOps:
             self.lib.eva_peer_free(ctypes.c_void_p(self._own_arena))
         self.peers = None
 
-    def dispatch_peers(self, x, idx, w):
+    def dispatch_peers(self, x, idx, w, all_to_self=False):
         M = x.shape[0]
         counts = torch.empty(self.world, dtype=_I32, device=self.device)
         pos = torch.empty(self.world, M, dtype=_I32, device=self.device)
         rc = self.lib.eva_ep_dispatch_peers(ctypes.byref(self.peers), x.data_ptr(), M, idx.data_ptr(), w.data_ptr(),
-                                            counts.data_ptr(), pos.data_ptr(), self.status.data_ptr(), self._stream())
+                                            int(all_to_self), counts.data_ptr(), pos.data_ptr(),
+                                            self.status.data_ptr(), self._stream())
         _lib.check(rc, "eva_ep_dispatch_peers")
         return counts, pos
 
@@ -262,15 +269,24 @@ class CudaEpOps:
         _lib.check(self.lib.eva_ep_wait_rows(ctypes.byref(self.peers), self.status.data_ptr(), self._stream()),
                    "eva_ep_wait_rows")
 
-    def _experts_call(self, rw_ptr: int, out_ptr: int):
+    def _experts_call(self, rw_ptr: int, out_ptr: int, own_rows: int = -1):
+        """Experts of the arena rows; own_rows >= 0: this rank's own tokens (the first own_rows rows of
+        its own segment) also get the shared expert, in the same launch."""
         P = self.peers
         base = self._own_arena
-        rc = self.lib.eva_moe_experts(ctypes.byref(self.local_shape), base + P.off_x, 1, self._arena_rows,
-                                      base + P.off_sel, 0, rw_ptr, self._tables, None, self.ws_local.data_ptr(),
-                                      self.ws_local.numel(), out_ptr, None, self._stream())
+        if own_rows >= 0 and self._shared is not None:
+            rc = self.lib.eva_moe_experts_window(ctypes.byref(self.shared_shape), base + P.off_x, 1, self._arena_rows,
+                                                 base + P.off_sel, 0, rw_ptr, self._tables, self._shared,
+                                                 self.peers.rank * self.segment_rows, own_rows,
+                                                 self.ws_local.data_ptr(), self.ws_local.numel(), out_ptr, None,
+                                                 self._stream())
+        else:
+            rc = self.lib.eva_moe_experts(ctypes.byref(self.local_shape), base + P.off_x, 1, self._arena_rows,
+                                          base + P.off_sel, 0, rw_ptr, self._tables, None, self.ws_local.data_ptr(),
+                                          self.ws_local.numel(), out_ptr, None, self._stream())
         _lib.check(rc, "eva_moe_experts (arena)")
 
-    def experts_arena(self):
+    def experts_arena(self, own_rows: int = -1):
         """Routed experts of every received row, from this rank's arena into its partial rows.
 
         With expert residency, the experts the received rows select are made resident first (misses
@@ -281,14 +297,14 @@ class CudaEpOps:
         base = self._own_arena
         res = self.residency
         if res is None:
-            self._experts_call(base + P.off_rw, base + P.off_part)
+            self._experts_call(base + P.off_rw, base + P.off_part, own_rows)
         else:
             active = self.recv_rw != 0
             needed = torch.unique(self.recv_sel[active]).tolist()      # host synchronisation
             groups = [needed[i:i + res.n_slots] for i in range(0, len(needed), res.n_slots)] or [[]]
             if len(groups) == 1:
                 res.ensure(groups[0])
-                self._experts_call(base + P.off_rw, base + P.off_part)
+                self._experts_call(base + P.off_rw, base + P.off_part, own_rows)
                 res.mark_used()
             else:
                 keep = torch.zeros(self.layer.n_local, dtype=torch.bool, device=self.device)
@@ -298,7 +314,8 @@ class CudaEpOps:
                     keep.zero_()
                     keep[torch.as_tensor(g, device=self.device)] = True
                     rw_g = torch.where(keep[self.recv_sel.long()], self.recv_rw, 0.0)
-                    self._experts_call(rw_g.data_ptr(), (self.part if gi == 0 else tmp).data_ptr())
+                    self._experts_call(rw_g.data_ptr(), (self.part if gi == 0 else tmp).data_ptr(),
+                                       own_rows if gi == 0 else -1)
                     res.mark_used()
                     if gi:
                         self.part.add_(tmp)
@@ -411,10 +428,13 @@ class EPMoE:
         if out is None:
             out = torch.empty(M, cfg.hidden, dtype=_BF16, device=self.device)
         if self.transport == "peers":
-            _, pos = ops.dispatch_peers(x, idx, w)
-            base = ops.shared(x)                  # overlaps the peers' dispatch
+            fuse = ops.has_shared
+            _, pos = ops.dispatch_peers(x, idx, w, all_to_self=fuse)
+            base = None
+            if not fuse:
+                base = ops.shared(x)
             ops.wait_rows()
-            ops.experts_arena()
+            ops.experts_arena(own_rows=M if fuse else -1)   # own tokens' shared expert in the same launch
             ops.combine_peers(pos, base, out, out_f32)
             return out
         seg = self.max_tokens if self.mode == "fixed" else 0

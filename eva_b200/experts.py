@@ -144,6 +144,19 @@ def _record_seed(seed: int, index: int) -> int:
     return (seed * 1_000_003 + index + 1) & 0x7FFF_FFFF_FFFF_FFFF
 
 
+def make_router(cfg: MoEConfig, device="cpu", seed: int = 0, router_scale: float = 0.02, bias_std: float | None = None):
+    """The synthetic layer's router: FP32 weights [E, H] from `seed`, bias [E] from `seed + 2`."""
+    rgen = torch.Generator(device="cpu")
+    rgen.manual_seed(seed)
+    router_w = (torch.randn(cfg.n_experts, cfg.hidden, generator=rgen) * router_scale).to(device)
+    bgen = torch.Generator(device="cpu")
+    bgen.manual_seed(seed + 2)
+    if bias_std is None:
+        bias_std = 0.01 if cfg.router != "softmax" else 0.0
+    router_b = (torch.randn(cfg.n_experts, generator=bgen) * bias_std).to(device)
+    return router_w, router_b
+
+
 def make_layer(cfg: MoEConfig, device="cpu", seed: int = 0, svh_scale: float = 0.02,
                router_scale: float = 0.02, bias_std: float | None = None,
                n_fill: int | None = None, experts=None) -> ExpertLayer:
@@ -176,14 +189,7 @@ def make_layer(cfg: MoEConfig, device="cpu", seed: int = 0, svh_scale: float = 0
         soffs, _, sshapes = record_layout(cfg.hidden, cfg.shared_inter, cfg.shared_bits)
         gen.manual_seed(_record_seed(seed, cfg.n_experts))
         _fill_record(storage, len(ids) * rec, soffs, sshapes, gen, svh_scale, device)
-    rgen = torch.Generator(device="cpu")
-    rgen.manual_seed(seed)
-    router_w = (torch.randn(cfg.n_experts, cfg.hidden, generator=rgen) * router_scale).to(device)
-    bgen = torch.Generator(device="cpu")
-    bgen.manual_seed(seed + 2)
-    if bias_std is None:
-        bias_std = 0.01 if cfg.router != "softmax" else 0.0
-    router_b = (torch.randn(cfg.n_experts, generator=bgen) * bias_std).to(device)
+    router_w, router_b = make_router(cfg, device, seed, router_scale, bias_std)
     packed, shared = _pointer_tables(cfg, storage, rec, len(ids))
     return ExpertLayer(cfg, storage, rec, packed.to(device), None if shared is None else shared.to(device),
                        router_w, router_b, ids)

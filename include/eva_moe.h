@@ -126,6 +126,16 @@ int eva_moe_experts_prefill(const EvaMoeShape* shape, const void* x, int32_t x_i
                             const int64_t* const* tables, const int64_t* shared,
                             void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, void* stream);
 
+/* eva_moe_experts with the shared expert applied to rows shared_row0 .. shared_row0 + shared_rows - 1
+ * only (other rows get their routed experts alone; rows with neither are zero). An expert-parallel
+ * rank uses it to run its own tokens' shared expert in the same launch as the rows other ranks sent
+ * it (its own tokens are one contiguous segment of the received rows). */
+int eva_moe_experts_window(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
+                           const void* sel, int32_t sel_is_i64, const float* rw,
+                           const int64_t* const* tables, const int64_t* shared,
+                           int32_t shared_row0, int32_t shared_rows, void* workspace, size_t workspace_bytes,
+                           float* out_f32, void* out_bf16, void* stream);
+
 /* Whole layer: eva_moe_route + eva_moe_experts. idx_out / w_out / logits_out may be NULL. */
 int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
                     const float* router_w, const float* router_b,
@@ -234,10 +244,12 @@ int eva_peer_close(void* ptr);
 int eva_peer_free(void* ptr);
 
 /* Plan + pack: token rows (x [M][H], routes idx/w [M][topk]) stored into the destinations' arenas.
- * pos: int32 [world][M], the token's row within its segment at rank r (-1: not sent); counts: int32
- * [world]. EVA_STATUS_CAPACITY when a destination would get more than segment_rows rows (dropped). */
+ * all_to_self != 0: every token also goes to this rank (its own segment then holds all M tokens in
+ * order, for eva_moe_experts_window's shared expert). pos: int32 [world][M], the token's row within its
+ * segment at rank r (-1: not sent); counts: int32 [world]. EVA_STATUS_CAPACITY when a destination would
+ * get more than segment_rows rows (dropped). */
 int eva_ep_dispatch_peers(const EvaEpPeers* p, const void* x, int32_t M, const int32_t* idx, const float* w,
-                          int32_t* counts, int32_t* pos, int32_t* status, void* stream);
+                          int32_t all_to_self, int32_t* counts, int32_t* pos, int32_t* status, void* stream);
 /* Wait until every source's rows of this step are in this rank's arena. */
 int eva_ep_wait_rows(const EvaEpPeers* p, int32_t* status, void* stream);
 /* Publish this rank's partial sums of this step (after the experts launch that wrote part). */

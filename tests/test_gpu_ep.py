@@ -189,3 +189,41 @@ def test_ep_ranks_match_one_gpu(tmp_path, transport, mode, M):
     assert res["status"] == 0
     # 700 tokens: a rank may take the register-decode kernel where the whole layer takes the tensor-core one
     assert res["max_rel_err"] < (1e-4 if M <= 64 else 3e-3), res
+
+
+@pytest.mark.parametrize("M,row0,rows", [(40, 8, 17), (300, 64, 150), (300, 0, 0)])
+def test_shared_expert_row_window(M, row0, rows):
+    """eva_moe_experts_window: the shared expert only on rows row0 .. row0 + rows - 1 (decode and tensor-core
+    paths), against full calls with and without the shared expert."""
+    import ctypes
+    lib = _lib.load()
+    layer = make_layer(SMALL, DEV, seed=8)
+    rng = np.random.default_rng(M + row0)
+    sel, rw = _routes(rng, M, SMALL.n_experts, SMALL.topk, zero=0.2)
+    sel_d, rw_d = torch.as_tensor(sel, device=DEV), torch.as_tensor(rw, device=DEV)
+    x = torch.randn(M, SMALL.hidden, device=DEV).to(torch.bfloat16)
+    tables = _lib.table_array(tuple(layer.packed.unbind(0)))
+    shared = _lib.shared_array(layer.shared.tolist())
+    st = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for shape, sh, window in ((_lib.shape_of(SMALL, shared=False), None, None), (_lib.shape_of(SMALL), shared, None),
+                              (_lib.shape_of(SMALL), shared, (row0, rows))):
+        ws = torch.zeros(lib.eva_moe_workspace_bytes(ctypes.byref(shape), M), dtype=torch.uint8, device=DEV)
+        out = torch.full((M, SMALL.hidden), float("nan"), device=DEV)
+        if window is None:
+            rc = lib.eva_moe_experts(ctypes.byref(shape), x.data_ptr(), 1, M, sel_d.data_ptr(), 0, rw_d.data_ptr(),
+                                     tables, sh, ws.data_ptr(), ws.numel(), out.data_ptr(), None, st)
+        else:
+            rc = lib.eva_moe_experts_window(ctypes.byref(shape), x.data_ptr(), 1, M, sel_d.data_ptr(), 0,
+                                            rw_d.data_ptr(), tables, sh, window[0], window[1], ws.data_ptr(),
+                                            ws.numel(), out.data_ptr(), None, st)
+        _lib.check(rc, "experts")
+        outs.append(out)
+    torch.cuda.synchronize()
+    routed, full, win = outs
+    mask = torch.zeros(M, 1, device=DEV)
+    mask[row0:row0 + rows] = 1
+    expect = routed + (full - routed) * mask
+    assert torch.isfinite(win).all()
+    err = (win - expect).abs().max().item() / expect.abs().max().item()
+    assert err < 1e-4, err
