@@ -314,6 +314,13 @@ __device__ __forceinline__ LaneGrp lane_grp(int lane)
     return g;
 }
 
+__device__ __forceinline__ uint32_t imad_pack(uint32_t hi, uint32_t lo)
+{
+    uint32_t r;
+    asm("mad.lo.u32 %0, %1, 65536, %2;" : "=r"(r) : "r"(hi), "r"(lo));
+    return r;
+}
+
 template <int K>
 __device__ __forceinline__ void decode_raw(const uint32_t* tile, const LaneGrp& g, uint32_t (&a)[4])
 {
@@ -325,10 +332,12 @@ __device__ __forceinline__ void decode_raw(const uint32_t* tile, const LaneGrp& 
         h[3 - j] = mul1_sum((wb >> (j * K)) & 0xffffu);
         h[7 - j] = mul1_sum((wa >> (j * K)) & 0xffffu);
     }
-    a[0] = __byte_perm(h[0], h[1], 0x5410);
-    a[1] = __byte_perm(h[4], h[5], 0x5410);
-    a[2] = __byte_perm(h[2], h[3], 0x5410);
-    a[3] = __byte_perm(h[6], h[7], 0x5410);
+    // pack pairs with a multiply-add (FMA pipe) instead of a byte permute (ALU pipe, the busier one):
+    // h < 2^16, so hi * 2^16 + lo is the packed pair
+    a[0] = imad_pack(h[1], h[0]);
+    a[1] = imad_pack(h[5], h[4]);
+    a[2] = imad_pack(h[3], h[2]);
+    a[3] = imad_pack(h[7], h[6]);
 }
 
 // A fragment from the lane's two trellis words (word w0 high, w1 low): exact fp16 weights.
