@@ -38,19 +38,31 @@ constexpr int PF_BM = 128;                               // rows per CTA: one ha
 constexpr int PF_BN = 128;                               // weight columns decoded per CTA: half of N = 256
 constexpr int PF_BK = 64;
 constexpr int PF_PAIR_N = 2 * PF_BN;
-constexpr int PF_DEC = 16;                               // decoder warps
 constexpr int NT_PF = 8;                                 // 16-column tiles per 128-column chunk
-constexpr int PF_THREADS = (2 + PF_DEC) * 32;            // producer, MMA, 16 decoders
 constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;            // 16 KB
 constexpr int PF_T_BYTES = 4 * 8 * 32 * 4;               // 4 k-tile rows x 8 tiles x 32K bytes (K <= 4)
 constexpr int PF_STAGE = PF_A_BYTES + PF_B_BYTES + PF_T_BYTES;
-constexpr int PF_STAGES = 6;
 constexpr int PF_EPI_LD = 129;                           // padded row (floats) of the epilogue tiles
-constexpr size_t PF_SMEM = 1024 + static_cast<size_t>(PF_STAGES) * PF_STAGE + 256;
 static_assert(PF_TILE_ROWS == 2 * PF_BM, "a CTA pair covers one expert tile");
-static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PF_STAGES * PF_STAGE, "epilogue tiles reuse the ring");
-static_assert(PF_SMEM <= 227 * 1024, "shared memory per CTA");
+
+// Per-kernel shape of the CTA: decoder warps, ring stages, CTAs per SM. gate/up: 16 decoders, 6
+// stages, one CTA per SM (its 512 TMEM columns fill the SM). down: its main loop is short (K = I), so
+// two CTAs share an SM (256 TMEM columns, 8 decoders, 3 stages each) and one's epilogue overlaps the
+// other's main loop.
+template <int NDEC, int NSTAGE, int MINB>
+struct PfCfg {
+    static constexpr int dec = NDEC, stages = NSTAGE, min_blocks = MINB;
+    static constexpr int threads = (2 + NDEC) * 32;       // producer, MMA, decoders
+    static constexpr int tiles_per_dec = 32 / NDEC;        // of the 32 weight tiles of a k-block
+    static constexpr size_t smem = 1024 + static_cast<size_t>(NSTAGE) * PF_STAGE + 256;
+    static_assert(32 % NDEC == 0, "decoders split the 32 tiles of a k-block");
+    static_assert(smem * MINB <= 228 * 1024, "shared memory per SM");
+};
+using PfGateCfg = PfCfg<16, 6, 1>;
+using PfDownCfg = PfCfg<8, 3, 2>;
+static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PfGateCfg::stages * PF_STAGE, "epilogue tiles reuse the ring");
+static_assert(PF_BM * PF_EPI_LD * 4 <= PfDownCfg::stages * PF_STAGE, "epilogue tile reuses the ring");
 
 struct PfParams {
     int M, H, I, I_sh, topk, S_cap, n_local, K, K_sh, has_shared, imax, act_routed, act_shared;
@@ -281,14 +293,16 @@ struct PfLoop {
     uint32_t rank;           // 0 = leader (issues the MMAs)
 };
 
+template <int NS>
 struct PfBars {
-    uint64_t afull[PF_STAGES], tfull[PF_STAGES], bfull[PF_STAGES], empty[PF_STAGES], accb;
+    uint64_t afull[NS], tfull[NS], bfull[NS], empty[NS], accb;
 };
 
-template <int K>
-__device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBars& B, uint32_t tmem, int warp, int lane,
-                                            int* status)
+template <int K, class CFG>
+__device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBars<CFG::stages>& B, uint32_t tmem,
+                                            int warp, int lane, int* status)
 {
+    constexpr int PF_STAGES = CFG::stages, TPW = CFG::tiles_per_dec;
     const int total = L.nproj * L.nkb;
     constexpr uint32_t TROW = NT_PF * 32 * K;   // bytes of one k-tile row's 8 tiles
     if (warp == 0) {
@@ -345,15 +359,16 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         umma_commit_pair(mapa_rank(&B.accb, 0));
         umma_commit_pair(mapa_rank(&B.accb, 1));
     } else {
-        // decoders: warp d (0..15) takes k-tile row d / 4 of the block and tiles 2 (d % 4) .. +1
+        // decoders: warp d takes tiles TPW d .. TPW d + TPW - 1 of the block's 32 (k-tile row q / 8,
+        // 16-column tile q % 8)
         const int d = warp - 2;
-        const int ktl = d >> 2, nt0 = (d & 3) * 2;
+        const int ktl = (d * TPW) >> 3, nt0 = (d * TPW) & 7;
         const LaneDec ld = lane_dec<K>(lane);
         const uint32_t ring_s = smem_u32(ring);
         // swizzled offsets of the lane's 4 words in each of its 2 tiles (fixed for the whole loop)
-        uint32_t so[2][4];
+        uint32_t so[TPW][4];
 #pragma unroll
-        for (int t = 0; t < 2; ++t) {
+        for (int t = 0; t < TPW; ++t) {
             const int n = (nt0 + t) * 16 + (lane >> 2);   // output column within the chunk (B row)
             const int k = ktl * 16 + 2 * (lane & 3);      // k within the 64-wide block
             so[t][0] = sw128_off(n, k);
@@ -369,14 +384,14 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
                 const uint32_t stage_s = ring_s + st * PF_STAGE;
                 const uint32_t tr = stage_s + PF_A_BYTES + PF_B_BYTES + ktl * TROW;
                 const uint32_t bt = stage_s + PF_A_BYTES;
-                uint32_t w[2][2];
+                uint32_t w[TPW][2];
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
+                for (int t = 0; t < TPW; ++t) {
                     w[t][0] = lds32(tr + t * 32 * K + tw0);
                     w[t][1] = lds32(tr + t * 32 * K + tw1);
                 }
 #pragma unroll
-                for (int t = 0; t < 2; ++t) {
+                for (int t = 0; t < TPW; ++t) {
                     uint32_t a[4];
                     decode_afrag_words<K>(w[t][0], w[t][1], ld.off, a);
 #pragma unroll
@@ -407,8 +422,9 @@ __device__ __forceinline__ void pf_tmem_to_smem(uint32_t tmem, int col0, float* 
     }
 }
 
+template <int NS>
 struct PfSmem {
-    PfBars bars;
+    PfBars<NS> bars;
     uint32_t tmem;
 };
 
@@ -420,14 +436,15 @@ __device__ __forceinline__ uint8_t* pf_ring(uint8_t* raw)
 
 // Both CTAs of the pair: barriers, the pair's TMEM allocation (one warp per CTA, same warp), and a
 // cluster barrier so that no CTA signals the other's barriers before they exist.
-__device__ __forceinline__ void pf_setup(PfSmem& S, int warp, int ncols)
+template <class CFG>
+__device__ __forceinline__ void pf_setup(PfSmem<CFG::stages>& S, int warp, int ncols)
 {
     if (threadIdx.x == 0) {
-        PfBars& B = S.bars;
-        for (int i = 0; i < PF_STAGES; ++i) {
+        PfBars<CFG::stages>& B = S.bars;
+        for (int i = 0; i < CFG::stages; ++i) {
             mbar_init(&B.afull[i], 1);
             mbar_init(&B.tfull[i], 1);
-            mbar_init(&B.bfull[i], 2 * PF_DEC);
+            mbar_init(&B.bfull[i], 2 * CFG::dec);
             mbar_init(&B.empty[i], 1);
         }
         mbar_init(&B.accb, 1);
@@ -442,7 +459,8 @@ __device__ __forceinline__ void pf_setup(PfSmem& S, int warp, int ncols)
     tc_fence_after();
 }
 
-__device__ __forceinline__ void pf_teardown(PfSmem& S, int warp, int ncols)
+template <int NS>
+__device__ __forceinline__ void pf_teardown(PfSmem<NS>& S, int warp, int ncols)
 {
     tc_fence_before();
     cluster_sync_all();
@@ -456,11 +474,13 @@ __device__ __forceinline__ void pf_teardown(PfSmem& S, int warp, int ncols)
 // pf_gateup: gate and up of one (expert tile of up to 256 rows, 256 columns of I), CTA pair
 
 template <int KR, int KS>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, PfGateCfg::min_blocks)
     pf_gateup(const PfParams p, const __grid_constant__ CUtensorMap mg, const __grid_constant__ CUtensorMap mu)
 {
+    using CFG = PfGateCfg;
+    constexpr int PF_THREADS = CFG::threads;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ PfSmem S;
+    __shared__ PfSmem<CFG::stages> S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     PfTile t;
     if (!pf_tile(p, blockIdx.y, t)) return;               // both CTAs of the pair agree
@@ -472,7 +492,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
     constexpr int NCOLS = 2 * PF_PAIR_N;
-    pf_setup(S, warp, NCOLS);
+    pf_setup<CFG>(S, warp, NCOLS);
 
     PfLoop L;
     L.amap[0] = &mg;
@@ -486,8 +506,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     L.nkb = p.H / PF_BK;
     L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
     L.rank = rank;
-    if (Ke == KR) pf_mainloop<KR>(L, ring, S.bars, S.tmem, warp, lane, p.status);
-    else pf_mainloop<KS>(L, ring, S.bars, S.tmem, warp, lane, p.status);
+    if (Ke == KR) pf_mainloop<KR, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
+    else pf_mainloop<KS, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
 
     // epilogue: this CTA's 128 rows x the pair's 256 columns, one 128-column chunk at a time
     mbar_wait(&S.bars.accb, 0, p.status);
@@ -532,11 +552,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
 // pf_down: down projection of one (expert tile, 256 columns of H), weighted per-slot rows, CTA pair
 
 template <int KR, int KS>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, PfDownCfg::min_blocks)
     pf_down(const PfParams p, const __grid_constant__ CUtensorMap ma)
 {
+    using CFG = PfDownCfg;
+    constexpr int PF_THREADS = CFG::threads;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ PfSmem S;
+    __shared__ PfSmem<CFG::stages> S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     PfTile t;
     if (!pf_tile(p, blockIdx.y, t)) return;
@@ -546,7 +568,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     const int Ke = t.shared ? KS : KR;
     uint8_t* ring = pf_ring(smem_raw);
     constexpr int NCOLS = PF_PAIR_N;
-    pf_setup(S, warp, NCOLS);
+    pf_setup<CFG>(S, warp, NCOLS);
 
     PfLoop L;
     L.amap[0] = L.amap[1] = &ma;
@@ -558,8 +580,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     L.nkb = I_e / PF_BK;
     L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
     L.rank = rank;
-    if (Ke == KR) pf_mainloop<KR>(L, ring, S.bars, S.tmem, warp, lane, p.status);
-    else pf_mainloop<KS>(L, ring, S.bars, S.tmem, warp, lane, p.status);
+    if (Ke == KR) pf_mainloop<KR, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
+    else pf_mainloop<KS, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
 
     mbar_wait(&S.bars.accb, 0, p.status);
     tc_fence_after();
@@ -730,8 +752,8 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     pick<4, 3>(p.K, p.K_sh, kg, kd);
     pick<4, 4>(p.K, p.K_sh, kg, kd);
     if (!kg || !kd) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(kg, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(PF_SMEM));
-    if (e == cudaSuccess) e = cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(PF_SMEM));
+    cudaError_t e = cudaFuncSetAttribute(kg, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(PfGateCfg::smem));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(PfDownCfg::smem));
     if (e != cudaSuccess) return e;
 
     const long long rot_items = static_cast<long long>(rows) * (p.H / 128) * 2;
@@ -740,8 +762,8 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     const int max_tiles = (p.S_cap + PF_TILE_ROWS - 1) / PF_TILE_ROWS + p.n_local +
                           (p.has_shared ? (p.shn + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
     const int pairs_gu = (L.imax / 128 + 1) / 2;          // 256-column pairs of the widest I (odd: last pair half used)
-    kg<<<dim3(2 * pairs_gu, max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, mg, mu);
-    kd<<<dim3(2 * (p.H / 256), max_tiles), PF_THREADS, PF_SMEM, stream>>>(p, ma);
+    kg<<<dim3(2 * pairs_gu, max_tiles), PfGateCfg::threads, PfGateCfg::smem, stream>>>(p, mg, mu);
+    kd<<<dim3(2 * (p.H / 256), max_tiles), PfDownCfg::threads, PfDownCfg::smem, stream>>>(p, ma);
     const long long comb = static_cast<long long>(p.M) * (p.H / 128);
     pf_combine<<<static_cast<unsigned>((comb + 7) / 8), 256, 0, stream>>>(p);
     return cudaGetLastError();
