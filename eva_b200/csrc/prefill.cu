@@ -27,6 +27,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -243,38 +244,47 @@ __device__ __forceinline__ int pf_row_slot(const PfParams& p, int pos)
 // ---------------------------------------------------------------------------------------------
 // pf_rotate: warp per (sorted row, 128 chunk, projection)
 
-__global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
+// One (sorted row, projection): resolve the row's token and its expert's suh once, then every 128-column
+// chunk (independent loads, so several are in flight per warp).
+__device__ __forceinline__ void pf_rotate_row(const PfParams& p, int pos, int pj, int lane)
 {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nch = p.H / 128;
-    const long long item = static_cast<long long>(blockIdx.x) * 8 + warp;
-    const long long rows = static_cast<long long>(p.S_cap) + p.M;
-    if (item >= rows * nch * 2) return;
-    const int pos = static_cast<int>(item / (nch * 2));
-    const int rem = static_cast<int>(item % (nch * 2));
-    const int c = rem >> 1, pj = rem & 1;
     int tok;
     const __half* suh;
     if (pos >= p.S_cap) {
         tok = pos - p.S_cap;
-        if (!p.has_shared || tok < p.sh0 || tok >= p.sh0 + p.shn) return;
         suh = reinterpret_cast<const __half*>(p.sh[pj ? 4 : 1]);
     } else {
-        if (pos >= p.runs[2 + p.runs[0]]) return;   // past the active rows
         const int slot = p.runs[2 + p.S_cap + 1 + pos];
         tok = slot / p.topk;
         const long long e = p.sel64 ? static_cast<const long long*>(p.sel)[slot] : static_cast<const int*>(p.sel)[slot];
         suh = reinterpret_cast<const __half*>(p.tables[pj ? 4 : 1][e]);
     }
-    const int col = c * 128 + lane * 4;
-    float v[4], su[4];
-    load4_x(p.x, static_cast<size_t>(tok) * p.H + col, p.x_bf16, v);
-    load4_half_ro(suh + col, su);
+    __half* dst = (pj ? p.xu : p.xg) + static_cast<size_t>(pos) * p.H;
+    const size_t xrow = static_cast<size_t>(tok) * p.H;
+#pragma unroll 4
+    for (int col = lane * 4; col < p.H; col += 128) {
+        float v[4], su[4];
+        load4_x(p.x, xrow + col, p.x_bf16, v);
+        load4_half_ro(suh + col, su);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] *= su[i];
-    had128_warp(v, lane);
-    store4_half((pj ? p.xu : p.xg) + static_cast<size_t>(pos) * p.H + col, v);
+        for (int i = 0; i < 4; ++i) v[i] *= su[i];
+        had128_warp(v, lane);
+        store4_half(dst + col, v);
+    }
 }
+
+__global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
+{
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // items: (active sorted row, projection), then (shared-expert row, projection); grid-stride over warps
+    const int n_act = p.runs[2 + p.runs[0]];
+    const int n_items = 2 * (n_act + (p.has_shared ? p.shn : 0));
+    for (int item = blockIdx.x * 8 + warp; item < n_items; item += gridDim.x * 8) {
+        const int row = item >> 1, pj = item & 1;
+        pf_rotate_row(p, row < n_act ? row : p.S_cap + p.sh0 + (row - n_act), pj, lane);
+    }
+}
+
 
 // ---------------------------------------------------------------------------------------------
 // Shared main loop of the two GEMM kernels (one CTA of the pair).
@@ -612,13 +622,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
 // ---------------------------------------------------------------------------------------------
 // pf_combine: warp per (token, 128 chunk)
 
+__device__ __forceinline__ void pf_combine_item(const PfParams& p, int tok, int c, int lane);
+
 __global__ void __launch_bounds__(256) pf_combine(const PfParams p)
 {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nch = p.H / 128;
-    const long long item = static_cast<long long>(blockIdx.x) * 8 + warp;
-    if (item >= static_cast<long long>(p.M) * nch) return;
-    const int tok = static_cast<int>(item / nch), c = static_cast<int>(item % nch);
+    const long long n_items = static_cast<long long>(p.M) * nch;
+    for (long long item = static_cast<long long>(blockIdx.x) * 8 + warp; item < n_items;
+         item += static_cast<long long>(gridDim.x) * 8)
+        pf_combine_item(p, static_cast<int>(item / nch), static_cast<int>(item % nch), lane);
+}
+
+__device__ __forceinline__ void pf_combine_item(const PfParams& p, int tok, int c, int lane)
+{
     const int col = c * 128 + lane * 4;
     float o[4] = {0.f, 0.f, 0.f, 0.f};
     for (int k = 0; k < p.topk; ++k) {
@@ -756,8 +773,8 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kd, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(PfDownCfg::smem));
     if (e != cudaSuccess) return e;
 
-    const long long rot_items = static_cast<long long>(rows) * (p.H / 128) * 2;
-    pf_rotate<<<static_cast<unsigned>((rot_items + 7) / 8), 256, 0, stream>>>(p);
+    const int small_grid = num_sms() * 8;
+    pf_rotate<<<small_grid, 256, 0, stream>>>(p);
     // tile upper bound: sum over experts of ceil(n_e / T) <= S / T + E, plus the shared tiles
     const int max_tiles = (p.S_cap + PF_TILE_ROWS - 1) / PF_TILE_ROWS + p.n_local +
                           (p.has_shared ? (p.shn + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
@@ -765,7 +782,7 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     kg<<<dim3(2 * pairs_gu, max_tiles), PfGateCfg::threads, PfGateCfg::smem, stream>>>(p, mg, mu);
     kd<<<dim3(2 * (p.H / 256), max_tiles), PfDownCfg::threads, PfDownCfg::smem, stream>>>(p, ma);
     const long long comb = static_cast<long long>(p.M) * (p.H / 128);
-    pf_combine<<<static_cast<unsigned>((comb + 7) / 8), 256, 0, stream>>>(p);
+    pf_combine<<<static_cast<unsigned>(std::min<long long>((comb + 7) / 8, small_grid)), 256, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
