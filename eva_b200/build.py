@@ -14,8 +14,8 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libeva_moe.so"
-SOURCES = ["capi.cu", "routing.cu", "experts.cu", "prefill.cu", "noalloc.cu", "ep.cu", "stack.cu"]
-HEADERS = ["common.cuh", "internal.h"]
+SOURCES = ["capi.cu", "routing.cu", "router_tc.cu", "experts.cu", "prefill.cu", "noalloc.cu", "ep.cu", "stack.cu"]
+HEADERS = ["common.cuh", "internal.h", "tc.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -10,7 +10,7 @@ namespace eva {
 
 static size_t up256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
-WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split)
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split, bool routing)
 {
     WsLayout L{};
     L.max_rows = max_rows;
@@ -37,8 +37,6 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split)
     L.estart = take((E + 1) * 4);
     L.slot_act = take(S * 4);
     L.tok_expect = take(M * 4);
-    const size_t lrows = std::max(static_cast<size_t>(L.ks_router) * std::min<size_t>(M, 32), M);
-    L.logits = take(lrows * E * 4);
     L.idx = take(M * s.topk * 4);
     L.w = take(M * s.topk * 4);
     // fragment-layout copies of the GEMV inputs: rows padded by one stage (32 k-tile rows = 512
@@ -57,6 +55,11 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split)
     const size_t pa = allow_split ? std::min<size_t>(PARTA_ITEMS, R * L.nchA * 4) : 0;
     L.partA = take(pa * 2 * RUN_ROWS * 128 * 4);
     L.max_split = allow_split ? 4 : 1;
+    // router regions last, so that every other offset is the same with and without them
+    if (routing) {
+        L.logits = take(router_part_rows(max_rows, s.hidden, s.n_experts) * E * 4);
+        L.wsplit = take(max_rows >= ROUTER_TC_MIN_ROWS ? 3 * E * H * 2 : 0);
+    }
     L.total = o;
     return L;
 }
@@ -182,7 +185,10 @@ int eva_moe_route(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, in
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     float* part = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + L.logits);
     int ks = 1;
-    cudaError_t e = launch_router_logits(x, x_is_bf16 ? 1 : 0, M, shape->hidden, shape->n_experts, router_w, part, &ks, st);
+    void* wsplit = M >= ROUTER_TC_MIN_ROWS ? static_cast<uint8_t*>(workspace) + L.wsplit : nullptr;
+    int* status = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + L.status);
+    cudaError_t e = launch_router_logits(x, x_is_bf16 ? 1 : 0, M, shape->hidden, shape->n_experts, router_w, part, wsplit,
+                                         status, &ks, st);
     if (e != cudaSuccess) return EVA_ERR_CUDA;
     return cuda_status(launch_topk(*shape, part, ks, M, router_b, logits_out, idx_out, w_out, st));
 }
@@ -223,7 +229,7 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
         for (int i = 0; i < 9; ++i)
             if (shared[i] == 0 || (shared[i] & 15)) return EVA_ERR_INVALID;   // bulk copies need 16 B
     if (M == 0) return EVA_OK;
-    const WsLayout L = ws_layout(*shape, M, allow_split);
+    const WsLayout L = ws_layout(*shape, M, allow_split, /*routing=*/false);
     if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     PermuteArgs pa;

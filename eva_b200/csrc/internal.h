@@ -12,19 +12,22 @@ namespace eva {
 constexpr int RUN_ROWS = 8;          // slots of one expert per run (MMA N dimension)
 constexpr int PARTA_ITEMS = 4096;    // split-k partial buffers of the gate/up stage
 constexpr int ROUTER_KSLICE = 512;   // k elements per router GEMV warp
+constexpr int ROUTER_TC_MIN_ROWS = 33;   // tensor-core router GEMM from this many tokens (bf16 inputs)
 
 // Byte offsets of the workspace regions for calls of up to max_rows tokens.
 struct WsLayout {
     int max_rows, S, R, imax, nchA, nchH, ks_router;
     size_t status, counters, n_counters, runs, run_expert, estart, slot_act, tok_expect;
-    size_t logits, idx, w, xrot, act, dpart, partA, xsum, asum, total;
+    size_t logits, wsplit, idx, w, xrot, act, dpart, partA, xsum, asum, total;
     size_t tstart, pxg, pxu, pap;   // prefill: tile prefix, sorted rotated inputs, sorted down inputs
     int max_split;   // largest gate/up k-split the partial buffer allows (1 = none)
     int hpad, ipad;  // row widths (halves) of the fragment-layout input buffers (one stage of slack)
 };
 
-// allow_split = false leaves out the split-k partial buffer (gate/up items are then never split).
-WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split = true);
+// allow_split = false leaves out the split-k partial buffer (gate/up items are then never split);
+// routing = false leaves out the router's regions (weight split planes, slice partial logits), which
+// come last, so every other offset is the same either way.
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split = true, bool routing = true);
 
 // Counter block layout inside `counters` (int32 indices).
 struct CtrLayout {
@@ -32,8 +35,17 @@ struct CtrLayout {
 };
 CtrLayout ctr_layout(const WsLayout& L);
 
+// Router logits into `part` ([ks][M][E] slice partials, *ks_used slices). wsplit: 3 E H bf16 of
+// workspace for the tensor-core path (may be null: SIMT path); status: the workspace status word.
 cudaError_t launch_router_logits(const void* x, int x_bf16, int M, int H, int E, const float* W, float* part,
-                                 int* ks_used, cudaStream_t stream);
+                                 void* wsplit, int* status, int* ks_used, cudaStream_t stream);
+// Tensor-core router GEMM: k slices for M tokens (0: shape not handled; kper_out: k per slice),
+// partial-logit rows a workspace for up to max_rows tokens holds, and the launch.
+int router_tc_split(int M, int H, int E, int* kper_out);
+size_t router_part_rows(int max_rows, int H, int E);
+bool router_tc_usable(const void* x, int x_bf16, int M, int H, int E, const void* wsplit);
+cudaError_t launch_router_tc(const void* x, int M, int H, int E, const float* W, void* wsplit, float* part, int* status,
+                             int* ks_used, cudaStream_t stream);
 cudaError_t launch_topk(const EvaMoeShape& s, const float* part, int ks, int M, const float* bias,
                         float* logits_out, int32_t* idx, float* w, cudaStream_t stream);
 

@@ -53,7 +53,7 @@ extern "C" int eva_moe_experts_noalloc(const EvaMoeShape* shape, const void* x, 
     if (!shape || M < 0) return EVA_ERR_INVALID;
     if (eva_moe_workspace_bytes(shape, 1) == 0) return EVA_ERR_INVALID;
     if (M == 0) return EVA_OK;
-    const WsLayout L = ws_layout(*shape, M, /*allow_split=*/false);
+    const WsLayout L = ws_layout(*shape, M, /*allow_split=*/false, /*routing=*/false);
     if (L.total > EVA_NOALLOC_SCRATCH_BYTES) return EVA_ERR_WORKSPACE;   // too many rows for the fixed scratch
     void* base = nullptr;
     if (scratch_address(&base) != cudaSuccess) return EVA_ERR_CUDA;

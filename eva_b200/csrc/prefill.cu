@@ -23,15 +23,13 @@
 //   pf_down      down projection, epilogue H128 * svh * routing weight -> per-slot fp32 rows
 //   pf_combine   per token: slots in slot order, then the shared expert (as the coop B kernel,
 //                exl3_moe_coop_kernel.cuh:906-949) -> bf16 / fp32 output
-#include <cuda.h>
-#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <mutex>
 
 #include "common.cuh"
 #include "internal.h"
+#include "tc.cuh"
 
 namespace eva {
 
@@ -90,39 +88,7 @@ struct PfParams {
 };
 
 // ---------------------------------------------------------------------------------------------
-// tcgen05 / TMA helpers
-
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr)
-{
-    // K-major, 128B swizzle: 8-row core groups 1024 B apart (SBO), LBO unused (1), version 1
-    return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) | (static_cast<uint64_t>(1) << 16) |
-           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
-}
-
-// kind::f16 instruction descriptor: fp16 A and B (K-major), fp32 accumulator, M x N
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N)
-{
-    return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
-{
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
+// CTA-pair tcgen05 / TMA helpers
 
 // 2-D TMA load of this CTA's rows whose completion is counted on the pair leader's barrier
 // (bar: shared::cluster address). Plain per-CTA load, no cross-CTA delivery of data.
@@ -172,8 +138,6 @@ __device__ __forceinline__ void cluster_sync_all()
 {
     asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
-
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Explicit shared-space accesses for the decoders (generic accesses wait on the long scoreboard).
 __device__ __forceinline__ uint32_t lds32(uint32_t addr)
@@ -668,20 +632,6 @@ __device__ __forceinline__ void pf_combine_item(const PfParams& p, int tok, int 
 
 // ---------------------------------------------------------------------------------------------
 // host side
-
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-    });
-    return fn;
-}
 
 // fp16 [rows][cols] row-major, box 64 x 128, 128B swizzle
 static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols)

@@ -57,7 +57,8 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const void* __restrict
     }
 }
 
-// Router logits, large M: 64 tokens x 64 experts per CTA, k chunks of 32 through shared memory,
+// Router logits, large M when the tensor-core path does not apply (fp16 activations, H not a
+// multiple of 64): 64 tokens x 64 experts per CTA, k chunks of 32 through shared memory,
 // each thread 4 x 4 outputs; full sums (one slice).
 __global__ void __launch_bounds__(256) router_gemm_kernel(const void* __restrict__ x, int x_bf16, int M, int H, int E,
                                                           const float* __restrict__ W, float* __restrict__ out)
@@ -107,9 +108,11 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const void* __restrict
 }
 
 cudaError_t launch_router_logits(const void* x, int x_bf16, int M, int H, int E, const float* W, float* part,
-                                 int* ks_used, cudaStream_t stream)
+                                 void* wsplit, int* status, int* ks_used, cudaStream_t stream)
 {
-    if (M <= 32) {
+    if (router_tc_usable(x, x_bf16, M, H, E, wsplit))
+        return launch_router_tc(x, M, H, E, W, wsplit, part, status, ks_used, stream);
+    if (M < ROUTER_TC_MIN_ROWS) {
         const int KS = (H + ROUTER_KSLICE - 1) / ROUTER_KSLICE;
         *ks_used = KS;
         const int warps = E * KS;

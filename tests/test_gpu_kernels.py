@@ -108,12 +108,17 @@ def test_group_limited_ties_and_masking(lib, oracle):
     assert np.array_equal(idx[0], np.arange(8))
 
 
-@pytest.mark.parametrize("M", [1, 5, 32, 33, 200])
+@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
+@pytest.mark.parametrize("M", [1, 5, 32, 33, 200, 1000])
 @pytest.mark.parametrize("cfg", [C.V3, C.V2_LITE], ids=lambda c: c.name)
-def test_router_logits_and_indices(lib, oracle, cfg, M):
+def test_router_logits_and_indices(lib, oracle, cfg, M, x_dtype):
+    """M <= 32: k-sliced GEMV; larger bf16 batches: the tensor-core GEMM (three bf16 parts of each
+    FP32 weight, k slices summed by the top-k kernel); larger fp16 batches: the SIMT GEMM."""
+    if x_dtype == torch.float16 and M not in (5, 200):
+        pytest.skip("fp16 activations: one size per path")
     layer = make_layer(cfg.with_(n_experts=cfg.n_experts), "cpu", seed=0, n_fill=0)
     g = torch.Generator().manual_seed(1)
-    x = torch.randn(M, cfg.hidden, generator=g).to(torch.bfloat16)
+    x = torch.randn(M, cfg.hidden, generator=g).to(torch.bfloat16).to(x_dtype)
     xd = x.to(DEV)
     W = layer.router_w.to(DEV)
     b = layer.router_b.to(DEV)
@@ -122,11 +127,16 @@ def test_router_logits_and_indices(lib, oracle, cfg, M):
     logits = torch.empty(M, cfg.n_experts, device=DEV)
     idx = torch.empty(M, cfg.topk, dtype=torch.int32, device=DEV)
     w = torch.empty(M, cfg.topk, device=DEV)
-    _lib.check(lib.eva_moe_route(ctypes.byref(sh), xd.data_ptr(), 1, M, W.data_ptr(), b.data_ptr(), logits.data_ptr(),
-                                 idx.data_ptr(), w.data_ptr(), ws.data_ptr(), ws.numel(), stream()), "route")
+    _lib.check(lib.eva_moe_route(ctypes.byref(sh), xd.data_ptr(), int(x_dtype == torch.bfloat16), M, W.data_ptr(),
+                                 b.data_ptr(), logits.data_ptr(), idx.data_ptr(), w.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 stream()), "route")
     torch.cuda.synchronize()
     ref_logits = oracle.router_logits(x.float().numpy(), layer.router_w.numpy())
     assert np.allclose(logits.cpu().numpy(), ref_logits, rtol=1e-4, atol=1e-4)
+    # FP32-level accuracy: error within 2^-16 of the dot product's absolute sum (a weight rounded to
+    # one bf16 part would be off by up to 2^-9 of it)
+    abs_sum = np.abs(x.float().numpy().astype(np.float64)) @ np.abs(layer.router_w.numpy().astype(np.float64)).T
+    assert np.all(np.abs(logits.cpu().numpy() - ref_logits) <= abs_sum * 2.0**-16 + 1e-30)
     # given the kernel's own logits the selection is bit-exact
     ridx, rw = oracle.route(logits.cpu().numpy(), layer.router_b.numpy(), cfg)
     assert np.array_equal(idx.cpu().numpy(), ridx)
