@@ -233,16 +233,21 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
     if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     PermuteArgs pa;
+    const bool tensor = path == 2 || (path == 0 && M >= PREFILL_MIN_ROWS);
     fill_permute(pa, *shape, sel, sel_is_i64 ? 1 : 0, rw, M, M);
     for (int i = 0; i < 9; ++i) pa.tables[i] = tables[i];
     pa.runs = reinterpret_cast<int32_t*>(ws + L.runs);
-    pa.run_expert = reinterpret_cast<int32_t*>(ws + L.run_expert);
     pa.estart = reinterpret_cast<int32_t*>(ws + L.estart);
     pa.tstart = reinterpret_cast<int32_t*>(ws + L.tstart);
     pa.slot_act = reinterpret_cast<int32_t*>(ws + L.slot_act);
-    pa.tok_expect = reinterpret_cast<int32_t*>(ws + L.tok_expect);
-    pa.counters = reinterpret_cast<int32_t*>(ws + L.counters);
-    pa.n_counters = static_cast<int>(L.n_counters);
+    if (!tensor) {
+        // the fused decode kernel's run owners, arrival counts and work counters; the tensor-core
+        // path writes every output row in its combine and needs none of them
+        pa.run_expert = reinterpret_cast<int32_t*>(ws + L.run_expert);
+        pa.tok_expect = reinterpret_cast<int32_t*>(ws + L.tok_expect);
+        pa.counters = reinterpret_cast<int32_t*>(ws + L.counters);
+        pa.n_counters = static_cast<int>(L.n_counters);
+    }
     pa.status = reinterpret_cast<int32_t*>(ws + L.status);
     pa.out_f32 = out_f32;
     pa.out_bf16 = out_bf16;
@@ -269,7 +274,6 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
     ea.out_bf16 = out_bf16;
     ea.sh0 = shared_row0;
     ea.shn = shape->shared_inter ? shared_rows : 0;
-    const bool tensor = path == 2 || (path == 0 && M >= PREFILL_MIN_ROWS);
     return cuda_status(tensor ? launch_prefill(ea, st) : launch_experts(ea, st));
 }
 

@@ -206,46 +206,135 @@ __device__ __forceinline__ int pf_row_slot(const PfParams& p, int pos)
 }
 
 // ---------------------------------------------------------------------------------------------
-// pf_rotate: warp per (sorted row, 128 chunk, projection)
+// pf_rotate: four lanes per (projection, sorted row, 128-column chunk), eight chunks per warp.
+//
+// Lane r of a chunk's four holds elements n = 32 j + 8 r + e (j, e = 0..3, 0..7): its 16-byte loads
+// and stores are contiguous 64-byte runs per chunk. The 128-point Hadamard transform takes its
+// butterflies in the order of the index bits, 0 to 6, as had128_warp does (bits 0-2 and 5-6 in
+// registers, bits 3-4 by two shuffles): the same operations, so the same fp32 results, with 2
+// shuffle stages per 32 values instead of 5 per 4.
 
-// One (sorted row, projection): resolve the row's token and its expert's suh once, then every 128-column
-// chunk (independent loads, so several are in flight per warp).
-__device__ __forceinline__ void pf_rotate_row(const PfParams& p, int pos, int pj, int lane)
+// 8 consecutive activations (bf16 or fp16) as floats; al16: the address is 16-byte aligned
+__device__ __forceinline__ void load8_x(const void* x, size_t off, int is_bf16, bool al16, float (&v)[8])
 {
-    int tok;
-    const __half* suh;
-    if (pos >= p.S_cap) {
-        tok = pos - p.S_cap;
-        suh = reinterpret_cast<const __half*>(p.sh[pj ? 4 : 1]);
+    uint32_t w[4];
+    if (al16) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off));
+        w[0] = u.x, w[1] = u.y, w[2] = u.z, w[3] = u.w;
     } else {
-        const int slot = p.runs[2 + p.S_cap + 1 + pos];
-        tok = slot / p.topk;
-        const long long e = p.sel64 ? static_cast<const long long*>(p.sel)[slot] : static_cast<const int*>(p.sel)[slot];
-        suh = reinterpret_cast<const __half*>(p.tables[pj ? 4 : 1][e]);
+        const uint2 u0 = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + off));
+        const uint2 u1 = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(x) + off + 4));
+        w[0] = u0.x, w[1] = u0.y, w[2] = u1.x, w[3] = u1.y;
     }
-    __half* dst = (pj ? p.xu : p.xg) + static_cast<size_t>(pos) * p.H;
-    const size_t xrow = static_cast<size_t>(tok) * p.H;
-#pragma unroll 4
-    for (int col = lane * 4; col < p.H; col += 128) {
-        float v[4], su[4];
-        load4_x(p.x, xrow + col, p.x_bf16, v);
-        load4_half_ro(suh + col, su);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] *= su[i];
-        had128_warp(v, lane);
-        store4_half(dst + col, v);
+    for (int i = 0; i < 4; ++i) {
+        if (is_bf16) {
+            v[2 * i] = __uint_as_float(w[i] << 16);
+            v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        } else {
+            const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+            v[2 * i] = __low2float(h);
+            v[2 * i + 1] = __high2float(h);
+        }
     }
 }
 
 __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
 {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // items: (active sorted row, projection), then (shared-expert row, projection); grid-stride over warps
+    const int lane = threadIdx.x & 31, q = lane >> 2, r = lane & 3;
     const int n_act = p.runs[2 + p.runs[0]];
-    const int n_items = 2 * (n_act + (p.has_shared ? p.shn : 0));
-    for (int item = blockIdx.x * 8 + warp; item < n_items; item += gridDim.x * 8) {
-        const int row = item >> 1, pj = item & 1;
-        pf_rotate_row(p, row < n_act ? row : p.S_cap + p.sh0 + (row - n_act), pj, lane);
+    const int n_rows = n_act + (p.has_shared ? p.shn : 0);
+    const int nch = p.H / 128;
+    const long long per_proj = static_cast<long long>(n_rows) * nch;
+    const long long n_units = 2 * per_proj;   // (projection, row, chunk), chunk fastest
+    const bool al16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
+    const long long warps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+    for (long long u0 = ((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * 8; u0 < n_units;
+         u0 += warps * 8) {
+        const long long u = u0 + q;
+        const bool valid = u < n_units;   // the lanes of a past-the-end chunk still take part in the shuffles
+        float v[32];
+        int pj = 0, pos = 0, c = 0;
+        if (valid) {
+            pj = u >= per_proj;
+            const long long rem = u - pj * per_proj;
+            const int row = static_cast<int>(rem / nch);
+            c = static_cast<int>(rem - static_cast<long long>(row) * nch);
+            pos = row < n_act ? row : p.S_cap + p.sh0 + (row - n_act);
+            int tok;
+            const __half* suh;
+            if (pos >= p.S_cap) {
+                tok = pos - p.S_cap;
+                suh = reinterpret_cast<const __half*>(p.sh[pj ? 4 : 1]);
+            } else {
+                const int slot = p.runs[2 + p.S_cap + 1 + pos];
+                tok = slot / p.topk;
+                const long long e = p.sel64 ? static_cast<const long long*>(p.sel)[slot] : static_cast<const int*>(p.sel)[slot];
+                suh = reinterpret_cast<const __half*>(p.tables[pj ? 4 : 1][e]);
+            }
+            const size_t xoff = static_cast<size_t>(tok) * p.H + c * 128 + r * 8;
+            const __half* sp = suh + c * 128 + r * 8;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float xv[8];
+                load8_x(p.x, xoff + j * 32, p.x_bf16, al16, xv);
+                const uint4 su = __ldg(reinterpret_cast<const uint4*>(sp + j * 32));
+                const uint32_t sw[4] = {su.x, su.y, su.z, su.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const __half2 h = *reinterpret_cast<const __half2*>(&sw[i]);
+                    v[j * 8 + 2 * i] = xv[2 * i] * __low2float(h);
+                    v[j * 8 + 2 * i + 1] = xv[2 * i + 1] * __high2float(h);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+        }
+        // index bits 0-2: e
+#pragma unroll
+        for (int h = 1; h < 8; h <<= 1)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if ((i & h) == 0) {
+                    const float a = v[i], b = v[i + h];
+                    v[i] = a + b;
+                    v[i + h] = a - b;
+                }
+        // index bits 3-4: r (lane bits 0-1)
+#pragma unroll
+        for (int m = 1; m < 4; m <<= 1) {
+            const bool upper = (r & m) != 0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
+                v[i] = upper ? (o - v[i]) : (v[i] + o);
+            }
+        }
+        // index bits 5-6: j
+#pragma unroll
+        for (int h = 8; h < 32; h <<= 1)
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if ((i & h) == 0) {
+                    const float a = v[i], b = v[i + h];
+                    v[i] = a + b;
+                    v[i + h] = a - b;
+                }
+        if (valid) {
+            const float sc = 0.08838834764831845f;   // 1/sqrt(128)
+            __half* dst = (pj ? p.xu : p.xg) + static_cast<size_t>(pos) * p.H + c * 128 + r * 8;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t w[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const __half2 h = __floats2half2_rn(v[j * 8 + 2 * i] * sc, v[j * 8 + 2 * i + 1] * sc);
+                    w[i] = *reinterpret_cast<const uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(dst + j * 32) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+        }
     }
 }
 
