@@ -340,6 +340,31 @@ __device__ __forceinline__ void decode_raw(const uint32_t* tile, const LaneGrp& 
     a[3] = imad_pack(h[7], h[6]);
 }
 
+// A fragment of one tile for a lane from the words of its two window groups (see LaneGrp): each
+// group is one funnel shift, each window one shift + mask; exact fp16 weights (the codebook FMA on
+// the packed pairs).
+template <int K>
+__device__ __forceinline__ void decode_afrag_grp(uint32_t b0, uint32_t b1, uint32_t a0, uint32_t a1, const LaneGrp& g,
+                                                 uint32_t (&a)[4])
+{
+    const uint32_t wb = __funnelshift_r(b1, b0, g.shb);
+    const uint32_t wa = __funnelshift_r(a1, a0, g.sha);
+    uint32_t h[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        h[3 - j] = mul1_sum((wb >> (j * K)) & 0xffffu);
+        h[7 - j] = mul1_sum((wa >> (j * K)) & 0xffffu);
+    }
+    const __half2 k0 = __halves2half2(__ushort_as_half(0x1eee), __ushort_as_half(0x1eee));
+    const __half2 k1 = __halves2half2(__ushort_as_half(0xc931), __ushort_as_half(0xc931));
+    const uint32_t p[4] = {imad_pack(h[1], h[0]), imad_pack(h[5], h[4]), imad_pack(h[3], h[2]), imad_pack(h[7], h[6])};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&p[i]), k0, k1);
+        a[i] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+}
+
 // A fragment from the lane's two trellis words (word w0 high, w1 low): exact fp16 weights.
 template <int K>
 __device__ __forceinline__ void decode_afrag_words(uint32_t w0, uint32_t w1, int off, uint32_t (&a)[4])

@@ -426,7 +426,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         // 16-column tile q % 8)
         const int d = warp - 2;
         const int ktl = (d * TPW) >> 3, nt0 = (d * TPW) & 7;
-        const LaneDec ld = lane_dec<K>(lane);
+        const LaneGrp lg = lane_grp<K>(lane);
         const uint32_t ring_s = smem_u32(ring);
         // swizzled offsets of the lane's 4 words in each of its 2 tiles (fixed for the whole loop)
         uint32_t so[TPW][4];
@@ -439,7 +439,8 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             so[t][2] = sw128_off(n, k + 8);
             so[t][3] = sw128_off(n + 8, k + 8);
         }
-        const uint32_t tw0 = nt0 * 32 * K + ld.w0 * 4, tw1 = nt0 * 32 * K + ld.w1 * 4;
+        const uint32_t tb0 = nt0 * 32 * K + lg.b0 * 4, tb1 = nt0 * 32 * K + lg.b1 * 4;
+        const uint32_t ta0 = nt0 * 32 * K + lg.a0 * 4, ta1 = nt0 * 32 * K + lg.a1 * 4;
         for (int s = 0; s < total; ++s) {
             const int st = s % PF_STAGES;
             mbar_wait(&B.tfull[st], (s / PF_STAGES) & 1, status);
@@ -447,16 +448,18 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
                 const uint32_t stage_s = ring_s + st * PF_STAGE;
                 const uint32_t tr = stage_s + PF_A_BYTES + PF_B_BYTES + ktl * TROW;
                 const uint32_t bt = stage_s + PF_A_BYTES;
-                uint32_t w[TPW][2];
+                uint32_t w[TPW][4];
 #pragma unroll
                 for (int t = 0; t < TPW; ++t) {
-                    w[t][0] = lds32(tr + t * 32 * K + tw0);
-                    w[t][1] = lds32(tr + t * 32 * K + tw1);
+                    w[t][0] = lds32(tr + t * 32 * K + tb0);
+                    w[t][1] = lds32(tr + t * 32 * K + tb1);
+                    w[t][2] = lds32(tr + t * 32 * K + ta0);
+                    w[t][3] = lds32(tr + t * 32 * K + ta1);
                 }
 #pragma unroll
                 for (int t = 0; t < TPW; ++t) {
                     uint32_t a[4];
-                    decode_afrag_words<K>(w[t][0], w[t][1], ld.off, a);
+                    decode_afrag_grp<K>(w[t][0], w[t][1], w[t][2], w[t][3], lg, a);
 #pragma unroll
                     for (int r = 0; r < 4; ++r) sts32(bt + so[t][r], a[r]);
                 }
