@@ -41,27 +41,32 @@ constexpr int NT_PF = 8;                                 // 16-column tiles per 
 constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;            // 16 KB
 constexpr int PF_T_BYTES = 4 * 8 * 32 * 4;               // 4 k-tile rows x 8 tiles x 32K bytes (K <= 4)
-constexpr int PF_STAGE = PF_A_BYTES + PF_B_BYTES + PF_T_BYTES;
 constexpr int PF_EPI_LD = 129;                           // padded row (floats) of the epilogue tiles
 static_assert(PF_TILE_ROWS == 2 * PF_BM, "a CTA pair covers one expert tile");
 
-// Per-kernel shape of the CTA: decoder warps, ring stages, CTAs per SM. gate/up: 16 decoders, 6
-// stages, one CTA per SM (its 512 TMEM columns fill the SM). down: its main loop is short (K = I), so
-// two CTAs share an SM (256 TMEM columns, 8 decoders, 3 stages each) and one's epilogue overlaps the
-// other's main loop.
-template <int NDEC, int NSTAGE, int MINB>
+// Per-kernel shape of the CTA: decoder warps, ring stages, CTAs per SM, 64-deep k blocks per stage.
+// Each decoder warp takes 4 weight tiles per stage: with fewer, the per-stage waits and barrier
+// arrivals cost a larger share of its time and its decode has less independent work in flight.
+//   gate/up: one CTA per SM (its 512 TMEM columns fill the SM), 16 decoders, 3 stages of 128-deep
+//            k blocks (two 64-deep halves each)
+//   down:    its main loop is short (K = I), so two CTAs share an SM (256 TMEM columns, 8 decoders,
+//            3 stages of 64-deep k blocks each) and one's epilogue overlaps the other's main loop
+template <int NDEC, int NSTAGE, int MINB, int KSUB>
 struct PfCfg {
-    static constexpr int dec = NDEC, stages = NSTAGE, min_blocks = MINB;
+    static constexpr int dec = NDEC, stages = NSTAGE, min_blocks = MINB, ksub = KSUB;
     static constexpr int threads = (2 + NDEC) * 32;       // producer, MMA, decoders
-    static constexpr int tiles_per_dec = 32 / NDEC;        // of the 32 weight tiles of a k-block
-    static constexpr size_t smem = 1024 + static_cast<size_t>(NSTAGE) * PF_STAGE + 256;
-    static_assert(32 % NDEC == 0, "decoders split the 32 tiles of a k-block");
+    static constexpr int tiles_per_dec = 32 * KSUB / NDEC;  // of the 32 KSUB weight tiles of a stage
+    static constexpr int a_bytes = KSUB * PF_A_BYTES;     // KSUB 64-deep activation sub-tiles
+    static constexpr int b_bytes = KSUB * PF_B_BYTES;     // KSUB 64-deep weight sub-tiles
+    static constexpr int stage = a_bytes + b_bytes + KSUB * PF_T_BYTES;
+    static constexpr size_t smem = 1024 + static_cast<size_t>(NSTAGE) * stage + 256;
+    static_assert((32 * KSUB) % NDEC == 0 && 8 % (32 * KSUB / NDEC) == 0, "a decoder's tiles lie in one k-tile row");
     static_assert(smem * MINB <= 228 * 1024, "shared memory per SM");
 };
-using PfGateCfg = PfCfg<16, 6, 1>;
-using PfDownCfg = PfCfg<8, 3, 2>;
-static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PfGateCfg::stages * PF_STAGE, "epilogue tiles reuse the ring");
-static_assert(PF_BM * PF_EPI_LD * 4 <= PfDownCfg::stages * PF_STAGE, "epilogue tile reuses the ring");
+using PfGateCfg = PfCfg<16, 3, 1, 2>;
+using PfDownCfg = PfCfg<8, 3, 2, 1>;
+static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PfGateCfg::stages * PfGateCfg::stage, "epilogue tiles reuse the ring");
+static_assert(PF_BM * PF_EPI_LD * 4 <= PfDownCfg::stages * PfDownCfg::stage, "epilogue tile reuses the ring");
 
 struct PfParams {
     int M, H, I, I_sh, topk, S_cap, n_local, K, K_sh, has_shared, imax, act_routed, act_shared;
@@ -343,7 +348,7 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
 // Shared main loop of the two GEMM kernels (one CTA of the pair).
 //   nproj   projections accumulated (gate+up: 2, down: 1); projection j accumulates into TMEM
 //           columns 256 j .. 256 j + 255
-//   nkb     k-blocks (64) per projection
+//   nkb     stages (k blocks of 64 ksub) per projection
 //   amap    tensor maps of the activation rows per projection; trellis bases per projection
 //   chunk   the 128-column weight chunk this CTA decodes (dec_valid = 0: past the end, not decoded)
 
@@ -365,7 +370,8 @@ template <int K, class CFG>
 __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBars<CFG::stages>& B, uint32_t tmem,
                                             int warp, int lane, int* status)
 {
-    constexpr int PF_STAGES = CFG::stages, TPW = CFG::tiles_per_dec;
+    constexpr int PF_STAGES = CFG::stages, TPW = CFG::tiles_per_dec, KSUB = CFG::ksub;
+    constexpr int PF_STAGE = CFG::stage, A_BYTES = CFG::a_bytes, B_BYTES = CFG::b_bytes;
     const int total = L.nproj * L.nkb;
     constexpr uint32_t TROW = NT_PF * 32 * K;   // bytes of one k-tile row's 8 tiles
     if (warp == 0) {
@@ -379,15 +385,18 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             const int pj = s / L.nkb, kb = s % L.nkb;
             uint8_t* stage = ring + st * PF_STAGE;
             if (lane == 0) {
-                if (L.rank == 0) mbar_arrive_expect_tx(&B.afull[st], 2 * PF_A_BYTES);
-                tma_load_2d_pair(stage, pj ? L.amap[1] : L.amap[0], kb * PF_BK, L.row0, mapa_rank(&B.afull[st], 0));
-                if (L.dec_valid) mbar_arrive_expect_tx(&B.tfull[st], 4 * TROW);
+                if (L.rank == 0) mbar_arrive_expect_tx(&B.afull[st], 2 * A_BYTES);
+#pragma unroll
+                for (int j = 0; j < KSUB; ++j)
+                    tma_load_2d_pair(stage + j * PF_A_BYTES, pj ? L.amap[1] : L.amap[0], (kb * KSUB + j) * PF_BK, L.row0,
+                                     mapa_rank(&B.afull[st], 0));
+                if (L.dec_valid) mbar_arrive_expect_tx(&B.tfull[st], 4 * KSUB * TROW);
                 else mbar_arrive(&B.tfull[st]);
             }
             __syncwarp();
-            if (L.dec_valid && lane < 4)
-                bulk_g2s(stage + PF_A_BYTES + PF_B_BYTES + lane * TROW,
-                         (pj ? L.trellis[1] : L.trellis[0]) + static_cast<size_t>(kb * 4 + lane) * L.row_stride +
+            if (L.dec_valid && lane < 4 * KSUB)
+                bulk_g2s(stage + A_BYTES + B_BYTES + lane * TROW,
+                         (pj ? L.trellis[1] : L.trellis[0]) + static_cast<size_t>(kb * 4 * KSUB + lane) * L.row_stride +
                              static_cast<size_t>(L.chunk) * TROW,
                          TROW, &B.tfull[st]);
             __syncwarp();
@@ -404,11 +413,13 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             mbar_wait(&B.bfull[st], ph, status);
             tc_fence_after();
             const uint32_t sa = smem_u32(ring + st * PF_STAGE);
-            const uint32_t sb = sa + PF_A_BYTES;
+            const uint32_t sb = sa + A_BYTES;
 #pragma unroll
-            for (int k = 0; k < PF_BK / 16; ++k)
-                umma_f16_pair(tmem + pj * PF_PAIR_N, umma_desc_sw128(sa + k * 32), umma_desc_sw128(sb + k * 32), idesc,
-                              (kb > 0 || k > 0) ? 1u : 0u);
+            for (int j = 0; j < KSUB; ++j)
+#pragma unroll
+                for (int k = 0; k < PF_BK / 16; ++k)
+                    umma_f16_pair(tmem + pj * PF_PAIR_N, umma_desc_sw128(sa + j * PF_A_BYTES + k * 32),
+                                  umma_desc_sw128(sb + j * PF_B_BYTES + k * 32), idesc, (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
             umma_commit_pair(smem_u32(&B.empty[st]));
             if (++kb == L.nkb) {
                 kb = 0;
@@ -422,22 +433,23 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         umma_commit_pair(mapa_rank(&B.accb, 0));
         umma_commit_pair(mapa_rank(&B.accb, 1));
     } else {
-        // decoders: warp d takes tiles TPW d .. TPW d + TPW - 1 of the block's 32 (k-tile row q / 8,
-        // 16-column tile q % 8)
+        // decoders: warp d takes tiles TPW d .. TPW d + TPW - 1 of the stage's 32 KSUB (k-tile row
+        // q / 8, 16-column tile q % 8); k-tile row ktl lies in 64-deep weight sub-tile ktl / 4
         const int d = warp - 2;
         const int ktl = (d * TPW) >> 3, nt0 = (d * TPW) & 7;
         const LaneGrp lg = lane_grp<K>(lane);
         const uint32_t ring_s = smem_u32(ring);
-        // swizzled offsets of the lane's 4 words in each of its 2 tiles (fixed for the whole loop)
+        // swizzled offsets of the lane's 4 words in each of its tiles (fixed for the whole loop)
         uint32_t so[TPW][4];
 #pragma unroll
         for (int t = 0; t < TPW; ++t) {
             const int n = (nt0 + t) * 16 + (lane >> 2);   // output column within the chunk (B row)
-            const int k = ktl * 16 + 2 * (lane & 3);      // k within the 64-wide block
-            so[t][0] = sw128_off(n, k);
-            so[t][1] = sw128_off(n + 8, k);
-            so[t][2] = sw128_off(n, k + 8);
-            so[t][3] = sw128_off(n + 8, k + 8);
+            const int k = (ktl & 3) * 16 + 2 * (lane & 3);  // k within the 64-deep sub-tile
+            const uint32_t sub = (ktl >> 2) * PF_B_BYTES;
+            so[t][0] = sub + sw128_off(n, k);
+            so[t][1] = sub + sw128_off(n + 8, k);
+            so[t][2] = sub + sw128_off(n, k + 8);
+            so[t][3] = sub + sw128_off(n + 8, k + 8);
         }
         const uint32_t tb0 = nt0 * 32 * K + lg.b0 * 4, tb1 = nt0 * 32 * K + lg.b1 * 4;
         const uint32_t ta0 = nt0 * 32 * K + lg.a0 * 4, ta1 = nt0 * 32 * K + lg.a1 * 4;
@@ -446,8 +458,8 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             mbar_wait(&B.tfull[st], (s / PF_STAGES) & 1, status);
             if (L.dec_valid) {
                 const uint32_t stage_s = ring_s + st * PF_STAGE;
-                const uint32_t tr = stage_s + PF_A_BYTES + PF_B_BYTES + ktl * TROW;
-                const uint32_t bt = stage_s + PF_A_BYTES;
+                const uint32_t tr = stage_s + A_BYTES + B_BYTES + ktl * TROW;
+                const uint32_t bt = stage_s + A_BYTES;
                 uint32_t w[TPW][4];
 #pragma unroll
                 for (int t = 0; t < TPW; ++t) {
@@ -569,7 +581,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
     L.chunk = 2 * pc + static_cast<int>(rank);
     L.dec_valid = L.chunk < nch;
     L.nproj = 2;
-    L.nkb = p.H / PF_BK;
+    L.nkb = p.H / (PF_BK * CFG::ksub);                     // H is a multiple of 128
     L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
     L.rank = rank;
     if (Ke == KR) pf_mainloop<KR, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
@@ -643,7 +655,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
     L.chunk = 2 * pc + static_cast<int>(rank);
     L.dec_valid = 1;                                       // H is a multiple of 256
     L.nproj = 1;
-    L.nkb = I_e / PF_BK;
+    L.nkb = I_e / (PF_BK * CFG::ksub);
     L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
     L.rank = rank;
     if (Ke == KR) pf_mainloop<KR, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
