@@ -41,6 +41,7 @@ constexpr int NT_PF = 8;                                 // 16-column tiles per 
 constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;            // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;            // 16 KB
 constexpr int PF_T_BYTES = 4 * 8 * 32 * 4;               // 4 k-tile rows x 8 tiles x 32K bytes (K <= 4)
+constexpr int PF_TSLOTS_MAX = 8;
 constexpr int PF_EPI_LD = 129;                           // padded row (floats) of the epilogue tiles
 static_assert(PF_TILE_ROWS == 2 * PF_BM, "a CTA pair covers one expert tile");
 
@@ -51,20 +52,23 @@ static_assert(PF_TILE_ROWS == 2 * PF_BM, "a CTA pair covers one expert tile");
 //            k blocks (two 64-deep halves each)
 //   down:    its main loop is short (K = I), so two CTAs share an SM (256 TMEM columns, 8 decoders,
 //            3 stages of 64-deep k blocks each) and one's epilogue overlaps the other's main loop
-template <int NDEC, int NSTAGE, int MINB, int KSUB>
+template <int NDEC, int NSTAGE, int MINB, int KSUB, int TSLOTS>
 struct PfCfg {
-    static constexpr int dec = NDEC, stages = NSTAGE, min_blocks = MINB, ksub = KSUB;
-    static constexpr int threads = (2 + NDEC) * 32;       // producer, MMA, decoders
+    static constexpr int dec = NDEC, stages = NSTAGE, min_blocks = MINB, ksub = KSUB, tslots = TSLOTS;
+    static constexpr int threads = (3 + NDEC) * 32;       // activation producer, MMA, decoders, trellis producer
     static constexpr int tiles_per_dec = 32 * KSUB / NDEC;  // of the 32 KSUB weight tiles of a stage
     static constexpr int a_bytes = KSUB * PF_A_BYTES;     // KSUB 64-deep activation sub-tiles
     static constexpr int b_bytes = KSUB * PF_B_BYTES;     // KSUB 64-deep weight sub-tiles
-    static constexpr int stage = a_bytes + b_bytes + KSUB * PF_T_BYTES;
-    static constexpr size_t smem = 1024 + static_cast<size_t>(NSTAGE) * stage + 256;
+    static constexpr int stage = a_bytes + b_bytes;
+    static constexpr int tslot = KSUB * PF_T_BYTES;       // trellis of one stage, in its own ring
+    static constexpr size_t ring_bytes = static_cast<size_t>(NSTAGE) * stage;
+    static constexpr size_t smem = 1024 + ring_bytes + static_cast<size_t>(TSLOTS) * tslot + 256;
+    static_assert(TSLOTS <= PF_TSLOTS_MAX, "trellis ring barriers");
     static_assert((32 * KSUB) % NDEC == 0 && 8 % (32 * KSUB / NDEC) == 0, "a decoder's tiles lie in one k-tile row");
     static_assert(smem * MINB <= 228 * 1024, "shared memory per SM");
 };
-using PfGateCfg = PfCfg<16, 3, 1, 2>;
-using PfDownCfg = PfCfg<8, 3, 2, 1>;
+using PfGateCfg = PfCfg<16, 3, 1, 2, 4>;
+using PfDownCfg = PfCfg<8, 3, 2, 1, 3>;
 static_assert(2 * PF_BM * PF_EPI_LD * 4 <= PfGateCfg::stages * PfGateCfg::stage, "epilogue tiles reuse the ring");
 static_assert(PF_BM * PF_EPI_LD * 4 <= PfDownCfg::stages * PfDownCfg::stage, "epilogue tile reuses the ring");
 
@@ -363,42 +367,56 @@ struct PfLoop {
 
 template <int NS>
 struct PfBars {
-    uint64_t afull[NS], tfull[NS], bfull[NS], empty[NS], accb;
+    uint64_t afull[NS], bfull[NS], empty[NS], accb;
+    uint64_t tfull[PF_TSLOTS_MAX], tempty[PF_TSLOTS_MAX];   // the trellis ring
 };
 
 template <int K, class CFG>
 __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBars<CFG::stages>& B, uint32_t tmem,
                                             int warp, int lane, int* status)
 {
-    constexpr int PF_STAGES = CFG::stages, TPW = CFG::tiles_per_dec, KSUB = CFG::ksub;
+    constexpr int PF_STAGES = CFG::stages, TPW = CFG::tiles_per_dec, KSUB = CFG::ksub, TS = CFG::tslots;
     constexpr int PF_STAGE = CFG::stage, A_BYTES = CFG::a_bytes, B_BYTES = CFG::b_bytes;
     const int total = L.nproj * L.nkb;
     constexpr uint32_t TROW = NT_PF * 32 * K;   // bytes of one k-tile row's 8 tiles
     if (warp == 0) {
-        // producer: own activation rows (counted on the leader's afull) and own trellis rows. The
-        // MMA commits each stage to the leader's empty barrier only; the leader's producer, once it
-        // sees a stage released, forwards the release to the peer CTA's barrier.
+        // activation producer: own activation rows (counted on the leader's afull). The MMA commits
+        // each stage to the leader's empty barrier only; the leader's producer, once it sees a stage
+        // released, forwards the release to the peer CTA's barrier.
         for (int s = 0; s < total; ++s) {
             const int st = s % PF_STAGES;
             mbar_wait(&B.empty[st], ((s / PF_STAGES) & 1) ^ 1, status);
-            if (L.rank == 0 && s >= PF_STAGES && lane == 0) mbar_arrive_remote(mapa_rank(&B.empty[st], 1));
-            const int pj = s / L.nkb, kb = s % L.nkb;
-            uint8_t* stage = ring + st * PF_STAGE;
             if (lane == 0) {
+                if (L.rank == 0 && s >= PF_STAGES) mbar_arrive_remote(mapa_rank(&B.empty[st], 1));
+                const int pj = s / L.nkb, kb = s % L.nkb;
+                uint8_t* stage = ring + st * PF_STAGE;
                 if (L.rank == 0) mbar_arrive_expect_tx(&B.afull[st], 2 * A_BYTES);
 #pragma unroll
                 for (int j = 0; j < KSUB; ++j)
                     tma_load_2d_pair(stage + j * PF_A_BYTES, pj ? L.amap[1] : L.amap[0], (kb * KSUB + j) * PF_BK, L.row0,
                                      mapa_rank(&B.afull[st], 0));
-                if (L.dec_valid) mbar_arrive_expect_tx(&B.tfull[st], 4 * KSUB * TROW);
-                else mbar_arrive(&B.tfull[st]);
+            }
+            __syncwarp();
+        }
+    } else if (warp == CFG::dec + 2) {
+        // trellis producer: own trellis rows, one bulk copy per k-tile row, into the trellis ring,
+        // whose slots the decoders release as soon as they have read them (so the copies run
+        // TSLOTS - 1 decode stages ahead, independent of the MMA)
+        uint8_t* tring = ring + CFG::ring_bytes;
+        for (int s = 0; s < total; ++s) {
+            const int ts = s % TS;
+            mbar_wait(&B.tempty[ts], ((s / TS) & 1) ^ 1, status);
+            const int pj = s / L.nkb, kb = s % L.nkb;
+            if (lane == 0) {
+                if (L.dec_valid) mbar_arrive_expect_tx(&B.tfull[ts], 4 * KSUB * TROW);
+                else mbar_arrive(&B.tfull[ts]);
             }
             __syncwarp();
             if (L.dec_valid && lane < 4 * KSUB)
-                bulk_g2s(stage + A_BYTES + B_BYTES + lane * TROW,
+                bulk_g2s(tring + ts * CFG::tslot + lane * TROW,
                          (pj ? L.trellis[1] : L.trellis[0]) + static_cast<size_t>(kb * 4 * KSUB + lane) * L.row_stride +
                              static_cast<size_t>(L.chunk) * TROW,
-                         TROW, &B.tfull[st]);
+                         TROW, &B.tfull[ts]);
             __syncwarp();
         }
     } else if (warp == 1) {
@@ -453,13 +471,13 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         }
         const uint32_t tb0 = nt0 * 32 * K + lg.b0 * 4, tb1 = nt0 * 32 * K + lg.b1 * 4;
         const uint32_t ta0 = nt0 * 32 * K + lg.a0 * 4, ta1 = nt0 * 32 * K + lg.a1 * 4;
+        const uint32_t tring = ring_s + static_cast<uint32_t>(CFG::ring_bytes) + ktl * TROW;
         for (int s = 0; s < total; ++s) {
-            const int st = s % PF_STAGES;
-            mbar_wait(&B.tfull[st], (s / PF_STAGES) & 1, status);
+            const int st = s % PF_STAGES, ts = s % TS;
+            mbar_wait(&B.tfull[ts], (s / TS) & 1, status);
+            uint32_t a[TPW][4];
             if (L.dec_valid) {
-                const uint32_t stage_s = ring_s + st * PF_STAGE;
-                const uint32_t tr = stage_s + A_BYTES + B_BYTES + ktl * TROW;
-                const uint32_t bt = stage_s + A_BYTES;
+                const uint32_t tr = tring + ts * CFG::tslot;
                 uint32_t w[TPW][4];
 #pragma unroll
                 for (int t = 0; t < TPW; ++t) {
@@ -469,12 +487,18 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
                     w[t][3] = lds32(tr + t * 32 * K + ta1);
                 }
 #pragma unroll
-                for (int t = 0; t < TPW; ++t) {
-                    uint32_t a[4];
-                    decode_afrag_grp<K>(w[t][0], w[t][1], w[t][2], w[t][3], lg, a);
+                for (int t = 0; t < TPW; ++t) decode_afrag_grp<K>(w[t][0], w[t][1], w[t][2], w[t][3], lg, a[t]);
+            }
+            // the words are in registers (the decode consumed them): release the trellis slot
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&B.tempty[ts]);
+            mbar_wait(&B.empty[st], ((s / PF_STAGES) & 1) ^ 1, status);   // the MMA is done with the ring stage
+            if (L.dec_valid) {
+                const uint32_t bt = ring_s + st * PF_STAGE + A_BYTES;
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) sts32(bt + so[t][r], a[r]);
-                }
+                for (int t = 0; t < TPW; ++t)
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) sts32(bt + so[t][r], a[t][r]);
                 fence_proxy_async_smem();
             }
             __syncwarp();
@@ -521,9 +545,12 @@ __device__ __forceinline__ void pf_setup(PfSmem<CFG::stages>& S, int warp, int n
         PfBars<CFG::stages>& B = S.bars;
         for (int i = 0; i < CFG::stages; ++i) {
             mbar_init(&B.afull[i], 1);
-            mbar_init(&B.tfull[i], 1);
             mbar_init(&B.bfull[i], 2 * CFG::dec);
             mbar_init(&B.empty[i], 1);
+        }
+        for (int i = 0; i < CFG::tslots; ++i) {
+            mbar_init(&B.tfull[i], 1);
+            mbar_init(&B.tempty[i], CFG::dec);
         }
         mbar_init(&B.accb, 1);
         fence_barrier_init();
