@@ -296,20 +296,29 @@ cudaError_t launch_topk(const EvaMoeShape& s, const float* part, int ks, int M, 
 
 constexpr int PERM_THREADS = 1024;
 
-__device__ __forceinline__ int slot_expert(const PermuteArgs& a, int s, bool flag_errors, int32_t* status)
+// Expert e's 9 table entries are all bound (non-zero) and 16-byte aligned (true without tables).
+__device__ __forceinline__ bool expert_bound(const PermuteArgs& a, int e)
 {
-    const int m = s / a.topk;
-    if (m >= a.M) return -1;
-    if (a.rw[s] == 0.0f) return -1;
-    const long long e = a.sel64 ? static_cast<const long long*>(a.sel)[s] : static_cast<const int32_t*>(a.sel)[s];
-    bool ok = e >= 0 && e < a.n_local;
-    if (ok && a.tables[0]) {
+    bool ok = true;
+    if (a.tables[0]) {
 #pragma unroll
         for (int r = 0; r < 9; ++r) {
             const int64_t p = a.tables[r][e];
             ok = ok && p != 0 && (p & 15) == 0;
         }
     }
+    return ok;
+}
+
+// bound: [E] per-expert expert_bound results (shared memory), filled before the first call
+__device__ __forceinline__ int slot_expert(const PermuteArgs& a, int s, bool flag_errors, int32_t* status,
+                                           const unsigned char* bound)
+{
+    const int m = s / a.topk;
+    if (m >= a.M) return -1;
+    if (a.rw[s] == 0.0f) return -1;
+    const long long e = a.sel64 ? static_cast<const long long*>(a.sel)[s] : static_cast<const int32_t*>(a.sel)[s];
+    const bool ok = e >= 0 && e < a.n_local && bound[e];
     if (!ok) {
         if (flag_errors && status) atomicOr(status, ST_BAD_EXPERT);
         return -1;
@@ -327,6 +336,7 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     int* tsh = rstart + E + 1;       // [E + 1] tile prefix
     int* cursor = tsh + E + 1;       // [E]
     int* wcnt = cursor + E;          // [32][E]
+    unsigned char* bound = reinterpret_cast<unsigned char*>(wcnt + 32 * E);   // [E]
     __shared__ int sh_tot[2];
     __shared__ int scan_tmp[32];
     __shared__ int scan_tmp2[32];
@@ -339,6 +349,7 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     for (int i = tid; i < E; i += PERM_THREADS) {
         hist[i] = 0;
         cursor[i] = 0;
+        bound[i] = expert_bound(a, i) ? 1 : 0;
     }
     if (a.counters)
         for (int i = tid; i < a.n_counters; i += PERM_THREADS) a.counters[i] = 0;
@@ -348,7 +359,7 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
 
     // 1. histogram
     for (int s = tid; s < S; s += PERM_THREADS) {
-        const int e = slot_expert(a, s, true, a.status);
+        const int e = slot_expert(a, s, true, a.status, bound);
         if (a.slot_act) a.slot_act[s] = e >= 0;
         if (e >= 0) {
             atomicAdd(&hist[e], 1);
@@ -412,7 +423,7 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     // 3. stable scatter
     for (int c0 = 0; c0 < S; c0 += PERM_THREADS) {
         const int s = c0 + tid;
-        const int e = s < S ? slot_expert(a, s, false, nullptr) : -1;
+        const int e = s < S ? slot_expert(a, s, false, nullptr, bound) : -1;
         const unsigned peers = __match_any_sync(0xffffffffu, e);
         const int rank = __popc(peers & ((1u << lane) - 1u));
         const bool leader = rank == 0;
@@ -484,7 +495,8 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
 
 cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t stream)
 {
-    const size_t smem = (static_cast<size_t>(a.n_local) * 5 + 3 + 32 * static_cast<size_t>(a.n_local)) * sizeof(int);
+    const size_t smem = (static_cast<size_t>(a.n_local) * 5 + 3 + 32 * static_cast<size_t>(a.n_local)) * sizeof(int) +
+                        static_cast<size_t>(a.n_local);
     cudaError_t e = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     permute_kernel<<<1, PERM_THREADS, smem, stream>>>(a);
