@@ -18,7 +18,7 @@ ACT_CLAMP_AFTER, ACT_CLAMP_BEFORE = 0, 1
 
 # every symbol include/eva_moe.h declares
 EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_status", "eva_moe_route",
-           "eva_moe_topk", "eva_moe_permute", "eva_moe_experts", "eva_moe_forward", "eva_exl3_dequant",
+           "eva_moe_topk", "eva_moe_permute", "eva_moe_permute_ws", "eva_moe_experts", "eva_moe_forward", "eva_exl3_dequant",
            "eva_moe_arch", "eva_moe_experts_noalloc", "eva_moe_experts_decode", "eva_moe_experts_prefill",
            "eva_ep_dispatch", "eva_ep_combine", "eva_ep_arena_layout", "eva_peer_alloc", "eva_peer_open",
            "eva_peer_close", "eva_peer_free", "eva_ep_dispatch_peers", "eva_ep_wait_rows", "eva_ep_signal_partials",
@@ -80,6 +80,8 @@ def load(build_if_missing: bool = True):
     L.eva_moe_topk.argtypes = [shp, vp, i32, vp, vp, vp, vp]
     L.eva_moe_permute.restype = ctypes.c_int
     L.eva_moe_permute.argtypes = [shp, vp, i32, vp, i32, i32, vp, vp, vp]
+    L.eva_moe_permute_ws.restype = ctypes.c_int
+    L.eva_moe_permute_ws.argtypes = [shp, vp, i32, vp, i32, i32, vp, vp, vp, sz, vp]
     L.eva_moe_experts.restype = ctypes.c_int
     L.eva_moe_experts.argtypes = [shp, vp, i32, i32, vp, i32, vp, P(vp), P(ctypes.c_int64), vp, sz, vp, vp, vp]
     for name in ("eva_moe_experts_decode", "eva_moe_experts_prefill"):

@@ -49,6 +49,7 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split, bool ro
     L.xsum = take(2 * St * L.nchH * 4);
     L.asum = take(St * L.nchA * 4);
     L.tstart = take((E + 2) * 4);
+    L.pscan = take(permute_scratch_ints(max_rows, static_cast<int>(E)) * 4);
     L.pxg = take(St * H * 2);
     L.pxu = take(St * H * 2);
     L.pap = take(St * L.imax * 2);
@@ -205,6 +206,24 @@ int eva_moe_permute(const EvaMoeShape* shape, const void* sel, int32_t sel_is_i6
     return cuda_status(launch_permute(pa, static_cast<cudaStream_t>(stream)));
 }
 
+int eva_moe_permute_ws(const EvaMoeShape* shape, const void* sel, int32_t sel_is_i64, const float* rw, int32_t M,
+                       int32_t capacity, int32_t* runs, int32_t* expert_start, void* workspace, size_t workspace_bytes,
+                       void* stream)
+{
+    if (!shape_ok(shape) || M < 0 || !sel || !rw || !runs || capacity < M || capacity < 1 || !workspace)
+        return EVA_ERR_INVALID;
+    if (static_cast<long long>(capacity) * shape->topk > 65535 * 16) return EVA_ERR_INVALID;
+    if (M == 0) return eva_moe_permute(shape, sel, sel_is_i64, rw, M, capacity, runs, expert_start, stream);
+    const WsLayout L = ws_layout(*shape, M, true, /*routing=*/false);
+    if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
+    PermuteArgs pa;
+    fill_permute(pa, *shape, sel, sel_is_i64 ? 1 : 0, rw, M, capacity);
+    pa.runs = runs;
+    pa.estart = expert_start;
+    pa.scratch = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + L.pscan);
+    return cuda_status(launch_permute(pa, static_cast<cudaStream_t>(stream)));
+}
+
 }  // extern "C"
 
 namespace eva {
@@ -240,6 +259,7 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
     pa.estart = reinterpret_cast<int32_t*>(ws + L.estart);
     pa.tstart = reinterpret_cast<int32_t*>(ws + L.tstart);
     pa.slot_act = reinterpret_cast<int32_t*>(ws + L.slot_act);
+    pa.scratch = reinterpret_cast<int32_t*>(ws + L.pscan);
     if (!tensor) {
         // the fused decode kernel's run owners, arrival counts and work counters; the tensor-core
         // path writes every output row in its combine and needs none of them

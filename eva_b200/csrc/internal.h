@@ -20,6 +20,7 @@ struct WsLayout {
     size_t status, counters, n_counters, runs, run_expert, estart, slot_act, tok_expect;
     size_t logits, wsplit, idx, w, xrot, act, dpart, partA, xsum, asum, total;
     size_t tstart, pxg, pxu, pap;   // prefill: tile prefix, sorted rotated inputs, sorted down inputs
+    size_t pscan;                   // multi-CTA permutation: per-chunk expert counts and prefixes
     int max_split;   // largest gate/up k-split the partial buffer allows (1 = none)
     int hpad, ipad;  // row widths (halves) of the fragment-layout input buffers (one stage of slack)
 };
@@ -67,8 +68,15 @@ struct PermuteArgs {
     int32_t* status;            // may be null
     float* out_f32;             // rows with no arrivals are zeroed (may be null)
     void* out_bf16;
+    int32_t* scratch;           // may be null: permute_scratch_ints(M, E) ints for the multi-CTA form
 };
 cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t stream);
+// Tokens per CTA of the multi-CTA permutation and the scratch it needs for M tokens, E experts.
+constexpr int PERM_TOK_CHUNK = 128;
+inline size_t permute_scratch_ints(int M, int E)
+{
+    return static_cast<size_t>((M + PERM_TOK_CHUNK - 1) / PERM_TOK_CHUNK) * E + 2 * (static_cast<size_t>(E) + 1) + 4;
+}
 
 struct ExpertsArgs {
     const EvaMoeShape* shape;

@@ -493,10 +493,222 @@ __global__ void __launch_bounds__(PERM_THREADS) permute_kernel(PermuteArgs a)
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Permutation, multi-CTA form for large batches: the same table in three launches.
+//   count:   CTA per chunk of PERM_TOK_CHUNK tokens (thread per token): per-chunk expert counts,
+//            slot_act, per-token arrival counts, work counters zeroed
+//   scan:    one CTA: per expert, the chunks' exclusive prefix (each chunk's base inside its
+//            expert's segment), then the expert / run / tile starts and the table header
+//   scatter: CTA per chunk: stable in-chunk ranks (as permute_kernel's step 3) from the chunk's
+//            bases, the table's zero tail, rows with no arrivals zeroed
+// Scratch (ints): [n_chunks][E] counts -> bases, [E + 1] slot starts, [E + 1] run starts.
+
+__global__ void __launch_bounds__(PERM_TOK_CHUNK) permute_count_kernel(PermuteArgs a)
+{
+    extern __shared__ int smem_i[];
+    const int E = a.n_local;
+    int* hist = smem_i;                                               // [E]
+    unsigned char* bound = reinterpret_cast<unsigned char*>(hist + E);   // [E]
+    const int tid = threadIdx.x, c = blockIdx.x;
+    for (int i = tid; i < E; i += blockDim.x) {
+        hist[i] = 0;
+        bound[i] = expert_bound(a, i) ? 1 : 0;
+    }
+    if (a.counters)
+        for (int i = blockIdx.x * blockDim.x + tid; i < a.n_counters; i += gridDim.x * blockDim.x) a.counters[i] = 0;
+    __syncthreads();
+    const int m = c * PERM_TOK_CHUNK + tid;
+    if (m < a.M) {
+        int n = 0;
+        for (int k = 0; k < a.topk; ++k) {
+            const int s = m * a.topk + k;
+            const int e = slot_expert(a, s, true, a.status, bound);
+            if (a.slot_act) a.slot_act[s] = e >= 0;
+            if (e >= 0) {
+                atomicAdd(&hist[e], 1);
+                ++n;
+            }
+        }
+        if (a.tok_expect) a.tok_expect[m] = n + ((a.has_shared && m >= a.sh0 && m < a.sh0 + a.shn) ? 1 : 0);
+    }
+    __syncthreads();
+    for (int i = tid; i < E; i += blockDim.x) a.scratch[static_cast<size_t>(c) * E + i] = hist[i];
+}
+
+__global__ void __launch_bounds__(PERM_THREADS) permute_scan_kernel(PermuteArgs a, int n_chunks)
+{
+    __shared__ int scan_tmp[3][32];
+    const int E = a.n_local;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int* sc_estart = a.scratch + static_cast<size_t>(n_chunks) * E;
+    int* sc_rstart = sc_estart + E + 1;
+    // per expert: exclusive prefix over the chunks (loads batched for memory-level parallelism)
+    int h = 0;
+    if (tid < E) {
+        int* col = a.scratch + tid;
+        int c = 0;
+        for (; c + 8 <= n_chunks; c += 8) {
+            int v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = col[static_cast<size_t>(c + i) * E];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                col[static_cast<size_t>(c + i) * E] = h;
+                h += v[i];
+            }
+        }
+        for (; c < n_chunks; ++c) {
+            const int v = col[static_cast<size_t>(c) * E];
+            col[static_cast<size_t>(c) * E] = h;
+            h += v;
+        }
+    }
+    // exclusive scans over experts (E <= 1024 = one element per thread): slots, runs, tiles
+    const int r = (h + RUN_ROWS - 1) / RUN_ROWS;
+    const int mt = (h + PF_TILE_ROWS - 1) / PF_TILE_ROWS;
+    int v0 = h, v1 = r, v2 = mt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n0 = __shfl_up_sync(0xffffffffu, v0, o);
+        const int n1 = __shfl_up_sync(0xffffffffu, v1, o);
+        const int n2 = __shfl_up_sync(0xffffffffu, v2, o);
+        if (lane >= o) {
+            v0 += n0;
+            v1 += n1;
+            v2 += n2;
+        }
+    }
+    if (lane == 31) {
+        scan_tmp[0][warp] = v0;
+        scan_tmp[1][warp] = v1;
+        scan_tmp[2][warp] = v2;
+    }
+    __syncthreads();
+    int b0 = 0, b1 = 0, b2 = 0, t0 = 0, t1 = 0, t2 = 0;
+    for (int w = 0; w < PERM_THREADS / 32; ++w) {
+        if (w < warp) {
+            b0 += scan_tmp[0][w];
+            b1 += scan_tmp[1][w];
+            b2 += scan_tmp[2][w];
+        }
+        t0 += scan_tmp[0][w];
+        t1 += scan_tmp[1][w];
+        t2 += scan_tmp[2][w];
+    }
+    if (tid < E) {
+        sc_estart[tid] = b0 + v0 - h;
+        sc_rstart[tid] = b1 + v1 - r;
+        if (a.estart) a.estart[tid] = b0 + v0 - h;
+        if (a.tstart) a.tstart[tid] = b2 + v2 - mt;
+    }
+    if (tid == 0) {
+        const int S_cap = a.capacity * a.topk;
+        sc_estart[E] = t0;
+        sc_rstart[E] = t1;
+        if (a.estart) a.estart[E] = t0;
+        if (a.tstart) {
+            a.tstart[E] = t2;
+            a.tstart[E + 1] = t2 + (a.has_shared ? (a.shn + PF_TILE_ROWS - 1) / PF_TILE_ROWS : 0);
+        }
+        a.runs[0] = t1;
+        a.runs[1] = 0;
+        a.runs[2 + t1] = t0;   // run_start[n_runs] = n_active
+        (void)S_cap;
+    }
+}
+
+__global__ void __launch_bounds__(PERM_THREADS) permute_scatter_kernel(PermuteArgs a, int n_chunks)
+{
+    extern __shared__ int smem_i[];
+    const int E = a.n_local;
+    int* cursor = smem_i;                 // [E] next position inside the expert's segment
+    int* wcnt = cursor + E;               // [32][E]
+    int* estart = wcnt + 32 * E;          // [E]
+    int* rstart = estart + E;             // [E]
+    unsigned char* bound = reinterpret_cast<unsigned char*>(rstart + E);   // [E]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, c = blockIdx.x;
+    const int* sc_estart = a.scratch + static_cast<size_t>(n_chunks) * E;
+    const int* sc_rstart = sc_estart + E + 1;
+    for (int i = tid; i < E; i += PERM_THREADS) {
+        cursor[i] = a.scratch[static_cast<size_t>(c) * E + i];
+        estart[i] = sc_estart[i];
+        rstart[i] = sc_rstart[i];
+        bound[i] = expert_bound(a, i) ? 1 : 0;
+    }
+    __syncthreads();
+    const int S_cap = a.capacity * a.topk;
+    const int S = a.M * a.topk;
+    int* run_start = a.runs + 2;
+    int* order = a.runs + 2 + S_cap + 1;
+    const int s_lo = c * PERM_TOK_CHUNK * a.topk, s_hi = min(S, s_lo + PERM_TOK_CHUNK * a.topk);
+    for (int c0 = s_lo; c0 < s_hi; c0 += PERM_THREADS) {
+        const int s = c0 + tid;
+        const int e = s < s_hi ? slot_expert(a, s, false, nullptr, bound) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        for (int i = tid; i < 32 * E; i += PERM_THREADS) wcnt[i] = 0;
+        __syncthreads();
+        if (rank == 0 && e >= 0) wcnt[warp * E + e] = __popc(peers);
+        __syncthreads();
+        for (int x = tid; x < E; x += PERM_THREADS) {
+            int run = cursor[x];
+            for (int w = 0; w < 32; ++w) {
+                const int v = wcnt[w * E + x];
+                wcnt[w * E + x] = run;
+                run += v;
+            }
+            cursor[x] = run;
+        }
+        __syncthreads();
+        if (e >= 0) {
+            const int pe = wcnt[warp * E + e] + rank;
+            const int pos = estart[e] + pe;
+            order[pos] = s;
+            if (pe % RUN_ROWS == 0) {
+                const int rid = rstart[e] + pe / RUN_ROWS;
+                run_start[rid] = pos;
+                if (a.run_expert) a.run_expert[rid] = e;
+            }
+        }
+        __syncthreads();
+    }
+    // the table's zero tail, over the whole grid
+    const int n_runs = sc_rstart[E], n_active = sc_estart[E];
+    const int gt = blockIdx.x * PERM_THREADS + tid, gs = gridDim.x * PERM_THREADS;
+    for (int i = n_runs + 1 + gt; i <= S_cap; i += gs) run_start[i] = 0;
+    for (int i = n_active + gt; i < S_cap; i += gs) order[i] = 0;
+    // rows nobody will write (no active slot, no shared expert) are zeroed; warp per row
+    if (a.tok_expect) {
+        const int m_hi = min(a.M, (c + 1) * PERM_TOK_CHUNK);
+        for (int m = c * PERM_TOK_CHUNK + warp; m < m_hi; m += PERM_THREADS / 32) {
+            if (a.tok_expect[m] != 0) continue;
+            const size_t row = static_cast<size_t>(m) * a.H;
+            if (a.out_f32)
+                for (int cc = lane * 4; cc < a.H; cc += 128)
+                    *reinterpret_cast<float4*>(a.out_f32 + row + cc) = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (a.out_bf16)
+                for (int cc = lane * 4; cc < a.H; cc += 128)
+                    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.out_bf16) + row + cc) = make_uint2(0, 0);
+        }
+    }
+}
+
 cudaError_t launch_permute(const PermuteArgs& a, cudaStream_t stream)
 {
-    const size_t smem = (static_cast<size_t>(a.n_local) * 5 + 3 + 32 * static_cast<size_t>(a.n_local)) * sizeof(int) +
-                        static_cast<size_t>(a.n_local);
+    const int E = a.n_local;
+    if (a.scratch && a.M > 2 * PERM_TOK_CHUNK) {
+        const int n_chunks = (a.M + PERM_TOK_CHUNK - 1) / PERM_TOK_CHUNK;
+        const size_t smem1 = static_cast<size_t>(E) * sizeof(int) + E;
+        const size_t smem3 = (static_cast<size_t>(E) * 35) * sizeof(int) + E;
+        cudaError_t e = cudaFuncSetAttribute(permute_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem3));
+        if (e != cudaSuccess) return e;
+        permute_count_kernel<<<n_chunks, PERM_TOK_CHUNK, smem1, stream>>>(a);
+        permute_scan_kernel<<<1, PERM_THREADS, 0, stream>>>(a, n_chunks);
+        permute_scatter_kernel<<<n_chunks, PERM_THREADS, smem3, stream>>>(a, n_chunks);
+        return cudaGetLastError();
+    }
+    const size_t smem = (static_cast<size_t>(E) * 5 + 3 + 32 * static_cast<size_t>(E)) * sizeof(int) + static_cast<size_t>(E);
     cudaError_t e = cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
     permute_kernel<<<1, PERM_THREADS, smem, stream>>>(a);

@@ -98,6 +98,14 @@ int eva_moe_topk(const EvaMoeShape* shape, const float* logits, int32_t M, const
 int eva_moe_permute(const EvaMoeShape* shape, const void* sel, int32_t sel_is_i64, const float* rw,
                     int32_t M, int32_t capacity, int32_t* runs, int32_t* expert_start, void* stream);
 
+/* The same table with a caller workspace (eva_moe_workspace_bytes for >= M rows): for batches above
+ * 256 tokens it is built by a multi-CTA form (per-chunk counts, one scan, per-chunk scatter) instead
+ * of one CTA. Same result, bit for bit. No counterpart in the reference (its prepare_routes is
+ * eva_moe_permute). */
+int eva_moe_permute_ws(const EvaMoeShape* shape, const void* sel, int32_t sel_is_i64, const float* rw,
+                       int32_t M, int32_t capacity, int32_t* runs, int32_t* expert_start, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
 /* Fused experts: permutation + rotation + gate/up + activation + down + routed combine + shared
  * expert, one persistent launch after the permutation.
  *   x:        [M][H] bf16 or fp16 (x_is_bf16)

@@ -150,15 +150,22 @@ def test_router_logits_and_indices(lib, oracle, cfg, M, x_dtype):
 # Permutation: bit-exact run table
 
 
-def _permute_gpu(lib, topk, n_local, sel, rw, capacity):
+def _permute_gpu(lib, topk, n_local, sel, rw, capacity, with_ws=False):
     cfg = C.MoEConfig("p", hidden=256, inter=128, n_experts=n_local, topk=topk, router="softmax")
     sh = _lib.shape_of(cfg, shared=False)
     seld = torch.tensor(np.asarray(sel, dtype=np.int64), device=DEV)
     rwd = torch.tensor(np.asarray(rw, dtype=np.float32), device=DEV)
     runs = torch.full((2 + 2 * capacity * topk + 1,), -7, dtype=torch.int32, device=DEV)
     est = torch.empty(n_local + 1, dtype=torch.int32, device=DEV)
-    _lib.check(lib.eva_moe_permute(ctypes.byref(sh), seld.data_ptr(), 1, rwd.data_ptr(), len(sel), capacity,
-                                   runs.data_ptr(), est.data_ptr(), stream()), "permute")
+    if with_ws:
+        ws = torch.full((lib.eva_moe_workspace_bytes(ctypes.byref(sh), max(len(sel), 1)),), 0x5A, dtype=torch.uint8,
+                        device=DEV)
+        _lib.check(lib.eva_moe_permute_ws(ctypes.byref(sh), seld.data_ptr(), 1, rwd.data_ptr(), len(sel), capacity,
+                                          runs.data_ptr(), est.data_ptr(), ws.data_ptr(), ws.numel(), stream()),
+                   "permute_ws")
+    else:
+        _lib.check(lib.eva_moe_permute(ctypes.byref(sh), seld.data_ptr(), 1, rwd.data_ptr(), len(sel), capacity,
+                                       runs.data_ptr(), est.data_ptr(), stream()), "permute")
     torch.cuda.synchronize()
     return runs.cpu().tolist(), est.cpu().numpy()
 
@@ -184,6 +191,25 @@ def test_permute_matches_oracle(lib, oracle, M, topk, E, zero):
     rw[rng.random((M, topk)) < zero] = 0
     runs, est = _permute_gpu(lib, topk, E, sel, rw, M)
     assert runs == oracle.run_table(sel, rw, M)
+    assert np.array_equal(est, oracle.expert_offsets(sel, rw, E))
+
+
+@pytest.mark.parametrize("M,topk,E,zero,cap_extra", [(257, 8, 256, 0.0, 0), (300, 8, 16, 0.05, 7), (1000, 6, 64, 0.2, 0),
+                                                     (4096, 8, 256, 0.02, 0), (5000, 8, 1024, 0.0, 33),
+                                                     (640, 12, 32, 0.5, 0)])
+def test_permute_multi_cta_matches_oracle(lib, oracle, M, topk, E, zero, cap_extra):
+    """Batches above 256 tokens with a workspace take the three-launch form (per-chunk counts, one
+    scan, per-chunk stable scatter): the same table as the one-CTA kernel and the oracle, bit for bit,
+    including ragged last chunks, inactive slots, spare capacity and top-k above 8 (two sub-chunks)."""
+    rng = np.random.default_rng(M + E + topk)
+    sel = np.stack([rng.choice(E, topk, replace=False) for _ in range(M)])
+    rw = rng.random((M, topk)).astype(np.float32) + 0.01
+    rw[rng.random((M, topk)) < zero] = 0
+    cap = M + cap_extra
+    runs, est = _permute_gpu(lib, topk, E, sel, rw, cap, with_ws=True)
+    runs1, est1 = _permute_gpu(lib, topk, E, sel, rw, cap)
+    assert runs == runs1 and np.array_equal(est, est1)
+    assert runs == oracle.run_table(sel, rw, cap)
     assert np.array_equal(est, oracle.expert_offsets(sel, rw, E))
 
 
