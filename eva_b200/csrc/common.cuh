@@ -365,32 +365,7 @@ __device__ __forceinline__ void decode_afrag_grp(uint32_t b0, uint32_t b1, uint3
     }
 }
 
-// A fragment from the lane's two trellis words (word w0 high, w1 low): exact fp16 weights.
-template <int K>
-__device__ __forceinline__ void decode_afrag_words(uint32_t w0, uint32_t w1, int off, uint32_t (&a)[4])
-{
-    const uint64_t v = (static_cast<uint64_t>(w0) << 32) | w1;
-    uint32_t st[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) st[j] = static_cast<uint32_t>(v >> (48 - off - j * K)) & 0xffffu;
-    a[0] = mul1_pair(st[0], st[1]);
-    a[1] = mul1_pair(st[4], st[5]);
-    a[2] = mul1_pair(st[2], st[3]);
-    a[3] = mul1_pair(st[6], st[7]);
-}
-
 // A fragment (4 x half2) of one tile for a lane: exact fp16 weights.
-template <int K>
-__device__ __forceinline__ void decode_afrag(const uint32_t* tile, const LaneDec& d, uint32_t (&a)[4])
-{
-    uint32_t st[8];
-    lane_states<K>(tile, d, st);
-    a[0] = mul1_pair(st[0], st[1]);
-    a[1] = mul1_pair(st[4], st[5]);
-    a[2] = mul1_pair(st[2], st[3]);
-    a[3] = mul1_pair(st[6], st[7]);
-}
-
 template <int K>
 __device__ __forceinline__ void decode_afrag(const uint32_t* tile, int lane, uint32_t (&a)[4])
 {
