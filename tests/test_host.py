@@ -115,3 +115,16 @@ def test_library_has_no_torch_dependency():
     import subprocess
     out = subprocess.run(["ldd", str(ROOT / "eva_b200" / "libeva_moe.so")], capture_output=True, text=True).stdout
     assert "torch" not in out and "c10" not in out
+
+
+def test_workspace_grows_with_the_row_count():
+    """A workspace sized for max_rows must serve every call with fewer rows: the size is
+    non-decreasing in the row count (the router's k-split and the permutation's chunk count both
+    depend on the row count; their regions are sized for the worst case up to max_rows)."""
+    from eva_b200 import _lib
+    L = _lib.load()
+    for cfg in (C.V3, C.V2_LITE, C.REF_NATIVE):
+        sh = _lib.shape_of(cfg)
+        rows = list(range(1, 300)) + list(range(300, 9000, 37))
+        sizes = [L.eva_moe_workspace_bytes(ctypes.byref(sh), m) for m in rows]
+        assert all(b >= a for a, b in zip(sizes, sizes[1:])), cfg.name
