@@ -341,9 +341,10 @@ __device__ __forceinline__ void decode_raw(const uint32_t* tile, const LaneGrp& 
 }
 
 // A fragment of one tile for a lane from the words of its two window groups (see LaneGrp): each
-// group is one funnel shift, each window one shift + mask; exact fp16 weights (the codebook FMA on
-// the packed pairs).
-template <int K>
+// group is one funnel shift, each window one shift + mask. RAW: the raw codebook values
+// h = 1024 + bytesum (exact fp16, as decode_raw; the affine map is applied to the products);
+// otherwise exact fp16 weights (the codebook FMA on the packed pairs).
+template <int K, bool RAW = false>
 __device__ __forceinline__ void decode_afrag_grp(uint32_t b0, uint32_t b1, uint32_t a0, uint32_t a1, const LaneGrp& g,
                                                  uint32_t (&a)[4])
 {
@@ -360,8 +361,12 @@ __device__ __forceinline__ void decode_afrag_grp(uint32_t b0, uint32_t b1, uint3
     const uint32_t p[4] = {imad_pack(h[1], h[0]), imad_pack(h[5], h[4]), imad_pack(h[3], h[2]), imad_pack(h[7], h[6])};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&p[i]), k0, k1);
-        a[i] = *reinterpret_cast<const uint32_t*>(&r);
+        if (RAW) {
+            a[i] = p[i];
+        } else {
+            const __half2 r = __hfma2(*reinterpret_cast<const __half2*>(&p[i]), k0, k1);
+            a[i] = *reinterpret_cast<const uint32_t*>(&r);
+        }
     }
 }
 

@@ -9,9 +9,12 @@
 // which is what bounds a tcgen05 kernel whose weights are written to shared memory by warps.
 //   warp 0      producer: 2-D TMA load of the CTA's activation rows (completion counted on the
 //               leader CTA's barrier) and 1-D bulk copies of its trellis rows, 6-stage ring
-//   warps 2-17  decoders: EXL3 decode of the k-block's 32 weight tiles (exact fp16, one rounding)
-//               straight into the UMMA K-major 128B-swizzled layout; they arrive on the leader's
-//               barrier (the peer CTA's from across the cluster)
+//   warps 2-17  decoders: EXL3 decode of the stage's weight tiles into raw codebook values
+//               h = 1024 + bytesum (exact fp16) straight into the UMMA K-major 128B-swizzled layout;
+//               they arrive on the leader's barrier (the peer CTA's from across the cluster). The
+//               codebook's affine map w = c0 h + c1 is applied in the epilogues: x . w = c0 (x . h)
+//               + c1 sum(x), with sum(x) over the row's stored fp16 inputs (pf_rotate and the gate/up
+//               epilogue write per-chunk partial sums)
 //   warp 1      leader CTA: one thread issues the pair MMAs and commits each stage to both CTAs
 //   all warps   epilogue: tcgen05.ld of the CTA's accumulators, Hadamard / scales / activation in
 //               registers, fp16 or fp32 stores.
@@ -90,6 +93,8 @@ struct PfParams {
     __half* xu;             // [S_cap + M][H] rotated up inputs
     __half* ap;             // [S_cap + M][imax] down inputs
     float* dpart;           // [S_cap + M][H] per-slot weighted down outputs
+    float* xsum;            // [2][S_cap + M][H / 128] sums of the stored fp16 gate / up inputs per 128 chunk
+    float* asum;            // [S_cap + M][imax / 128] sums of the stored fp16 down inputs per 128 chunk
     const int* slot_act;
     float* out_f32;
     __nv_bfloat16* out_bf16;
@@ -330,6 +335,7 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
                     v[i] = a + b;
                     v[i + h] = a - b;
                 }
+        float sm = 0.0f;   // sum of the values as stored (fp16), for the raw-codebook correction
         if (valid) {
             const float sc = 0.08838834764831845f;   // 1/sqrt(128)
             __half* dst = (pj ? p.xu : p.xg) + static_cast<size_t>(pos) * p.H + c * 128 + r * 8;
@@ -340,10 +346,14 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
                 for (int i = 0; i < 4; ++i) {
                     const __half2 h = __floats2half2_rn(v[j * 8 + 2 * i] * sc, v[j * 8 + 2 * i + 1] * sc);
                     w[i] = *reinterpret_cast<const uint32_t*>(&h);
+                    sm += __low2float(h) + __high2float(h);
                 }
                 *reinterpret_cast<uint4*>(dst + j * 32) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if (valid && r == 0) p.xsum[(static_cast<size_t>(pj) * (p.S_cap + p.M) + pos) * nch + c] = sm;
     }
 }
 
@@ -487,7 +497,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
                     w[t][3] = lds32(tr + t * 32 * K + ta1);
                 }
 #pragma unroll
-                for (int t = 0; t < TPW; ++t) decode_afrag_grp<K>(w[t][0], w[t][1], w[t][2], w[t][3], lg, a[t]);
+                for (int t = 0; t < TPW; ++t) decode_afrag_grp<K, true>(w[t][0], w[t][1], w[t][2], w[t][3], lg, a[t]);
             }
             // the words are in registers (the decode consumed them): release the trellis slot
             __syncwarp();
@@ -521,6 +531,26 @@ __device__ __forceinline__ void pf_tmem_to_smem(uint32_t tmem, int col0, float* 
         tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + col0 + c * 32, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) tile[row * PF_EPI_LD + c * 32 + i] = v[i];
+    }
+}
+
+// Row sums for the raw-codebook correction, gathered once per CTA in parallel (L threads per row,
+// each a fixed sequence of the row's per-chunk partial sums, then a fixed shuffle tree): out[r] =
+// sum over c < nchunk of part[(row0 + r) * stride + c] for the CTA's rows r < rows.
+template <int L>
+__device__ __forceinline__ void pf_row_sums(const float* part, size_t stride, int nchunk, int row0, int rows,
+                                            float* out, int nthreads)
+{
+    static_assert(L == 2 || L == 4, "threads per row");
+    for (int t0 = 0; t0 < PF_BM * L; t0 += nthreads) {
+        const int t = t0 + static_cast<int>(threadIdx.x);
+        const int r = t / L, q = t % L;
+        float s = 0.0f;
+        if (t < PF_BM * L && r < rows)
+            for (int c = q; c < nchunk; c += L) s += __ldcg(part + static_cast<size_t>(row0 + r) * stride + c);
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        if (L == 4) s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if (t < PF_BM * L && q == 0) out[r] = s;
     }
 }
 
@@ -621,6 +651,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
     float* U = G + PF_BM * PF_EPI_LD;
     const int rows = min(PF_BM, t.rows - static_cast<int>(rank) * PF_BM);
     const int mode = t.shared ? p.act_shared : p.act_routed;
+    // raw codebook: x . w = c0 (x . h) + c1 sum(x), sum(x) over the row's stored fp16 inputs
+    __shared__ float rsum[2][PF_BM];
+    {
+        const int nchH = p.H / 128;
+        if (threadIdx.x < PF_BM * 4) {
+            pf_row_sums<4>(p.xsum, nchH, nchH, L.row0, rows, rsum[0], PF_BM * 4);
+            pf_row_sums<4>(p.xsum + (static_cast<size_t>(p.S_cap) + p.M) * nchH, nchH, nchH, L.row0, rows, rsum[1], PF_BM * 4);
+        }
+    }
     for (int c = 0; c < 2; ++c) {
         const int chunk = 2 * pc + c;
         if (chunk >= nch) break;
@@ -635,18 +674,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
         load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 5)) + col, svu);
         load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 7)) + col, sud);
         for (int r = warp; r < rows; r += PF_THREADS / 32) {
+            const int pos = L.row0 + r;
+            const float sg = rsum[0][r], su = rsum[1][r];
             float g[4], u[4], a[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                g[i] = G[r * PF_EPI_LD + lane * 4 + i];
-                u[i] = U[r * PF_EPI_LD + lane * 4 + i];
+                g[i] = CB_C0 * G[r * PF_EPI_LD + lane * 4 + i] + CB_C1 * sg;
+                u[i] = CB_C0 * U[r * PF_EPI_LD + lane * 4 + i] + CB_C1 * su;
             }
             had128_warp(g, lane);
             had128_warp(u, lane);
 #pragma unroll
             for (int i = 0; i < 4; ++i) a[i] = act_gated(g[i] * svg[i], u[i] * svu[i], p.limit, mode) * sud[i];
             had128_warp(a, lane);
-            store4_half(p.ap + static_cast<size_t>(L.row0 + r) * p.imax + col, a);
+            store4_half(p.ap + static_cast<size_t>(pos) * p.imax + col, a);
+            float sa = 0.0f;   // sum of the values as stored (fp16), for the down projection's correction
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sa += __half2float(__float2half_rn(a[i]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sa += __shfl_xor_sync(0xffffffffu, sa, o);
+            if (lane == 0) p.asum[static_cast<size_t>(pos) * (p.imax / 128) + chunk] = sa;
         }
         __syncthreads();
     }
@@ -692,6 +739,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
     tc_fence_after();
     float* D = reinterpret_cast<float*>(ring);
     const int rows = min(PF_BM, t.rows - static_cast<int>(rank) * PF_BM);
+    // raw codebook correction with the sums of the rows' stored fp16 down inputs
+    __shared__ float rsum[PF_BM];
+    if (threadIdx.x < PF_BM * 2) pf_row_sums<2>(p.asum, p.imax / 128, I_e / 128, L.row0, rows, rsum, PF_BM * 2);
     for (int c = 0; c < 2; ++c) {
         if (warp < 4) pf_tmem_to_smem(S.tmem, c * PF_BN, D, warp, lane);
         __syncthreads();
@@ -701,9 +751,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
         for (int r = warp; r < rows; r += PF_THREADS / 32) {
             const int slot = pf_row_slot(p, L.row0 + r);
             const float w = t.shared ? 1.0f : p.rw[slot];
+            const float sa = rsum[r];
             float v[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] = D[r * PF_EPI_LD + lane * 4 + i];
+            for (int i = 0; i < 4; ++i) v[i] = CB_C0 * D[r * PF_EPI_LD + lane * 4 + i] + CB_C1 * sa;
             had128_warp(v, lane);
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[i] *= svd[i] * w;
@@ -828,6 +879,8 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     p.xu = reinterpret_cast<__half*>(ws + L.pxu);
     p.ap = reinterpret_cast<__half*>(ws + L.pap);
     p.dpart = reinterpret_cast<float*>(ws + L.dpart);
+    p.xsum = reinterpret_cast<float*>(ws + L.xsum);
+    p.asum = reinterpret_cast<float*>(ws + L.asum);
     p.slot_act = reinterpret_cast<const int*>(ws + L.slot_act);
     p.out_f32 = a.out_f32;
     p.out_bf16 = static_cast<__nv_bfloat16*>(a.out_bf16);
