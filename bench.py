@@ -99,6 +99,11 @@ def zipf_bias(cfg, base, seed=3):
     return (base + off).contiguous()
 
 
+# untimed prefill steps before the timed ones (the leg can follow seconds of CPU-only work, after
+# which the GPU clocks need a few steps to come back up)
+PREFILL_WARMUP = 5
+
+
 def prefill_measure(cfg, layer, dev, steps, warmup, M):
     """Prefill step (router + tensor-core experts) on M tokens with Zipf-skewed routing."""
     import ctypes
@@ -456,7 +461,7 @@ def ep_bench(args, cfg, dev, rank, world, local):
         xs = [torch.randn(P, cfg.hidden, device=dev, generator=g).to(torch.bfloat16) for _ in range(2)]
         out = torch.empty(P, cfg.hidden, dtype=torch.bfloat16, device=dev)
         idx = torch.empty(P, cfg.topk, dtype=torch.int32, device=dev)
-        for i in range(2):
+        for i in range(PREFILL_WARMUP):
             ep.forward(xs[i % 2], out=out, idx_out=idx)
         torch.cuda.synchronize()
         dist.barrier()
@@ -625,7 +630,7 @@ def main():
         return ep_bench(args, cfg, dev, rank, world, local)
     if args.prefill_only:
         layer = make_layer(cfg, dev, seed=0)
-        res = prefill_measure(cfg, layer, dev, max(1, min(args.steps, 10)), 2, args.prefill_tokens)
+        res = prefill_measure(cfg, layer, dev, max(1, min(args.steps, 10)), PREFILL_WARMUP, args.prefill_tokens)
         if rank == 0:
             print(json.dumps(res), flush=True)
         return
@@ -773,7 +778,7 @@ def main():
     if not args.no_prefill and world == 1:
         del moe
         torch.cuda.empty_cache()
-        prefill = prefill_measure(cfg, layer, dev, max(1, min(steps, 10)), 2, args.prefill_tokens)
+        prefill = prefill_measure(cfg, layer, dev, max(1, min(steps, 10)), PREFILL_WARMUP, args.prefill_tokens)
 
     tokens = M * steps * world
     line = {
