@@ -268,6 +268,14 @@ struct WarpItem {
     int slot[RUN_ROWS];
 };
 
+// Ring stage header written by the producer: the item and its stage, and at the item's first stage
+// its geometry, run and the run's slots (the producer has them already; the 16 consumer warps copy
+// them instead of each repeating the chain of dependent global loads).
+struct StageHdr {
+    int item, s;
+    WarpItem wi;
+};
+
 // Epilogue operands prefetched at item start by the warp that runs the epilogue of row `warp`:
 // type 1: svh_gate, svh_up, suh_down of the chunk; type 2: svh_down (fp16 x 4 per lane).
 struct EpiOps {
@@ -283,7 +291,7 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
     float* res = red + RED_FLOATS;   // [2][8][128]
     uint64_t* full = reinterpret_cast<uint64_t*>(res + RES_FLOATS);
     uint64_t* empty = full + NSTAGE;
-    int* hdr = reinterpret_cast<int*>(empty + NSTAGE);   // [NSTAGE][2] item, stage
+    __shared__ StageHdr hdr[NSTAGE];
     __shared__ WarpItem wis[NCW];
     __shared__ EpiOps eps[RUN_ROWS];
     __shared__ int sh_flag;
@@ -336,10 +344,17 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                           static_cast<size_t>(g.chunk) * row_bytes;
                 }
                 if (lane == 0) {
-                    hdr[slot * 2 + 0] = item;
-                    hdr[slot * 2 + 1] = s;
-                    mbar_arrive_expect_tx(&full[slot], nvalid * row_bytes);
+                    hdr[slot].item = item;
+                    hdr[slot].s = s;
+                    if (item >= 0 && s == 0) {
+                        hdr[slot].wi.g = g;
+                        hdr[slot].wi.ri = ri;
+                    }
                 }
+                if (item >= 0 && s == 0 && lane < RUN_ROWS)
+                    hdr[slot].wi.slot[lane] = lane < ri.nrows ? run_slot(p, g.run, lane) : run_slot(p, g.run, 0);
+                __syncwarp();
+                if (lane == 0) mbar_arrive_expect_tx(&full[slot], nvalid * row_bytes);
                 __syncwarp();
                 if (lane < nvalid)
                     bulk_g2s(ring + slot * (STAGE_BYTES / 4) + lane * (row_bytes / 4), src + lane * row_stride, row_bytes,
@@ -376,20 +391,20 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
         const int slot = q % NSTAGE;
         const uint32_t ph = (q / NSTAGE) & 1;
         mbar_wait(&full[slot], ph, p.status);
-        const int item = hdr[slot * 2 + 0];
-        const int s = hdr[slot * 2 + 1];
+        const int item = hdr[slot].item;
+        const int s = hdr[slot].s;
         if (item < 0) break;
         if (item != cur_item) {
             // item start, per warp: geometry, the run's slots, the dependency, epilogue prefetch
             cur_item = item;
             if (lane == 0) {
-                wi.g = item_geo(p, item);
-                wi.ri = run_info(p, wi.g.run);
+                wi.g = hdr[slot].wi.g;
+                wi.ri = hdr[slot].wi.ri;
             }
+            if (lane < RUN_ROWS) wi.slot[lane] = hdr[slot].wi.slot[lane];
             __syncwarp();
             const Geo g = wi.g;
             const RunInfo ri = wi.ri;
-            if (lane < RUN_ROWS) wi.slot[lane] = lane < ri.nrows ? run_slot(p, g.run, lane) : run_slot(p, g.run, 0);
             sp = 0;
             proj = 0;
             __syncwarp();
