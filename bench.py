@@ -102,6 +102,7 @@ def zipf_bias(cfg, base, seed=3):
 # untimed prefill steps before the timed ones (the leg can follow seconds of CPU-only work, after
 # which the GPU clocks need a few steps to come back up)
 PREFILL_WARMUP = 5
+PREFILL_WARMUP_S = 0.3
 
 
 def prefill_measure(cfg, layer, dev, steps, warmup, M):
@@ -137,8 +138,14 @@ def prefill_measure(cfg, layer, dev, steps, warmup, M):
         if ev is not None:
             ev[1].record()
 
-    for i in range(warmup):
+    # at least `warmup` untimed steps and at least PREFILL_WARMUP_S seconds of them
+    t_w = time.perf_counter()
+    i = 0
+    while i < warmup or time.perf_counter() - t_w < PREFILL_WARMUP_S:
         step(i)
+        i += 1
+        if i >= warmup:
+            torch.cuda.synchronize()
     torch.cuda.synchronize()
     loads = np.bincount(idx.cpu().numpy().ravel(), minlength=cfg.n_experts)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
