@@ -13,9 +13,9 @@
   (weights, indices) as `Block.route`, `experts(x)` routes, runs the routed experts and the shared
   expert and returns the result in x's dtype (BF16 hidden states in and out).
 
-Both run on the caller's current CUDA stream, never synchronise the host unless asked to
-(`check_bounds=True` reads the device status word after the launch), and accept being captured in
-a CUDA graph (no host synchronisation inside, fixed workspace).
+Both run on the caller's current CUDA stream and never synchronise the host unless asked to
+(`check_bounds=True` reads the device status word after the launch); a call allocates nothing and
+uses a workspace fixed at construction.
 """
 from __future__ import annotations
 
