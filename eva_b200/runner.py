@@ -14,8 +14,8 @@
   expert and returns the result in x's dtype (BF16 hidden states in and out).
 
 Both run on the caller's current CUDA stream and never synchronise the host unless asked to
-(`check_bounds=True` reads the device status word after the launch); a call allocates nothing and
-uses a workspace fixed at construction.
+(`check_bounds=True` reads the device status word after the launch); the library call itself uses
+the workspace fixed at construction, and only the returned tensors come from torch's allocator.
 """
 from __future__ import annotations
 
