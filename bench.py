@@ -280,12 +280,21 @@ def run_reference(args):
         times.append(dt)
     total = sum(times)
     value = args.steps / total
-    sample = f"1 token per step (FP64 router + its {cfg.topk} routed experts + shared expert, EXL3 dequantised)"
+    sample = (f"1 token per step of the batch-{args.batch} workload (FP64 router + its {cfg.topk} routed experts + "
+              f"shared expert, EXL3 dequantised), on rank 0's host cores")
+    world, M = args.gpus, args.batch
+    # the eva arm's config for the same run (bench.py decode line), the sample described in cpu_baseline
+    config = {"workload": f"DeepSeek-{cfg.name.upper()} MoE layer decode (EXL3 K{cfg.bits}), batch {M} tokens/step"
+                          + (f" per GPU, expert parallel over {world} GPUs" if world > 1 else ""),
+              "hidden": cfg.hidden, "experts": cfg.n_experts, "topk": cfg.topk, "inter": cfg.inter,
+              "shared_inter": cfg.shared_inter, "bits": cfg.bits, "batch": M,
+              "parallelism": f"ep{world}" if world > 1 else "single",
+              "reference_path": "the reference's path restated on the CPU (oracle port), rank 0"}
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * total / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} MoE layer decode, CPU restatement", "batch": 1},
+        "config": config,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
