@@ -128,3 +128,23 @@ def test_workspace_grows_with_the_row_count():
         rows = list(range(1, 300)) + list(range(300, 9000, 37))
         sizes = [L.eva_moe_workspace_bytes(ctypes.byref(sh), m) for m in rows]
         assert all(b >= a for a, b in zip(sizes, sizes[1:])), cfg.name
+
+
+def test_argument_errors_are_reported_without_a_gpu():
+    """Entry points validate their arguments and the workspace size before touching a device."""
+    from eva_b200 import _lib
+    L = _lib.load()
+    sh = _lib.shape_of(C.V3)
+    fake = 256   # never dereferenced: every call below fails its checks first
+    # permutation with a workspace: missing workspace, workspace too small for the rows
+    assert L.eva_moe_permute_ws(ctypes.byref(sh), fake, 1, fake, 300, 300, fake, None, None, 0, None) == _lib.EVA_ERR_INVALID
+    assert L.eva_moe_permute_ws(ctypes.byref(sh), fake, 1, fake, 300, 300, fake, None, fake, 1024, None) == \
+        _lib.EVA_ERR_WORKSPACE
+    # capacity below the row count
+    assert L.eva_moe_permute(ctypes.byref(sh), fake, 1, fake, 300, 299, fake, None, None) == _lib.EVA_ERR_INVALID
+    # routing: workspace too small for the rows (the router's slice partials and weight planes)
+    n = L.eva_moe_workspace_bytes(ctypes.byref(sh), 64)
+    assert L.eva_moe_route(ctypes.byref(sh), fake, 1, 65, fake, None, None, fake, fake, fake, n, None) == \
+        _lib.EVA_ERR_WORKSPACE
+    assert L.eva_moe_route(ctypes.byref(sh), fake, 1, 64, fake, None, None, fake, fake, None, n, None) == \
+        _lib.EVA_ERR_INVALID
