@@ -7,9 +7,11 @@
 // the tensor cores of both SMs read both halves, and each CTA's TMEM receives its 128 rows x 256
 // columns. Per SM this reads half the shared-memory bytes per MAC of a one-SM 128 x 128 tile,
 // which is what bounds a tcgen05 kernel whose weights are written to shared memory by warps.
-//   warp 0      producer: 2-D TMA load of the CTA's activation rows (completion counted on the
-//               leader CTA's barrier) and 1-D bulk copies of its trellis rows, 6-stage ring
-//   warps 2-17  decoders: EXL3 decode of the stage's weight tiles into raw codebook values
+//   warp 0      activation producer: 2-D TMA loads of the CTA's activation rows (completion counted
+//               on the leader CTA's barrier) into the activation/weight ring (PfCfg: stages, depth)
+//   last warp   trellis producer: 1-D bulk copies of the CTA's trellis rows into a ring of their
+//               own, whose slots the decoders release as soon as they have read their words
+//   warps 2..   decoders: EXL3 decode of the stage's weight tiles into raw codebook values
 //               h = 1024 + bytesum (exact fp16) straight into the UMMA K-major 128B-swizzled layout;
 //               they arrive on the leader's barrier (the peer CTA's from across the cluster). The
 //               codebook's affine map w = c0 h + c1 is applied in the epilogues: x . w = c0 (x . h)
