@@ -388,7 +388,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
                                             int warp, int lane, int* status)
 {
     constexpr int PF_STAGES = CFG::stages, TPW = CFG::tiles_per_dec, KSUB = CFG::ksub, TS = CFG::tslots;
-    constexpr int PF_STAGE = CFG::stage, A_BYTES = CFG::a_bytes, B_BYTES = CFG::b_bytes;
+    constexpr int PF_STAGE = CFG::stage, A_BYTES = CFG::a_bytes;
     const int total = L.nproj * L.nkb;
     constexpr uint32_t TROW = NT_PF * 32 * K;   // bytes of one k-tile row's 8 tiles
     if (warp == 0) {
