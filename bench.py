@@ -773,6 +773,13 @@ def main():
         except (IndexError, ValueError):
             traffic = None
 
+    # the prefill leg before the CPU baseline: the GPU is still busy from the decode leg
+    prefill = None
+    if not args.no_prefill and world == 1:
+        del moe
+        torch.cuda.empty_cache()
+        prefill = prefill_measure(cfg, layer, dev, max(1, min(steps, 10)), PREFILL_WARMUP, args.prefill_tokens)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from eva_b200.experts import replicate_experts
@@ -789,12 +796,6 @@ def main():
         cpu = {"value": len(ts) / sum(ts), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": f"{len(ts)} single-token steps (FP64 router + top-{cfg.topk} routed experts + shared, "
                          f"EXL3 dequantised by the C restatement)"}
-
-    prefill = None
-    if not args.no_prefill and world == 1:
-        del moe
-        torch.cuda.empty_cache()
-        prefill = prefill_measure(cfg, layer, dev, max(1, min(steps, 10)), PREFILL_WARMUP, args.prefill_tokens)
 
     tokens = M * steps * world
     line = {
