@@ -187,7 +187,10 @@ def route(logits: np.ndarray, bias: np.ndarray, cfg) -> tuple[np.ndarray, np.nda
     sqrtsoftplus: model.py:404-416. sigmoid: DeepSeek-V3 noaux_tc (group score = sum of the top-2
     biased scores of a group, top `topk_group` groups kept, others -inf). softmax: DeepSeek-V2-Lite
     greedy top-k. Weights are the unbiased scores, renormalised over the selection when
-    cfg.norm_topk (sum + 1e-20), times cfg.route_scale.
+    cfg.norm_topk (sum + 1e-20), times cfg.route_scale. Equal scores go to the lower expert id.
+    The sigmoid and softmax forms are checked against transformers 5.5.0
+    DeepseekV3MoE.route_tokens_to_experts and DeepseekV2Moe.route_tokens_to_experts ("greedy")
+    by tests/golden/make_route_pins.py.
     """
     s = scores(logits, cfg.router)
     M, E = s.shape

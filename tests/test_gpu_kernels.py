@@ -98,6 +98,19 @@ def test_topk_matches_reference_block_route(lib):
     assert np.allclose(w, g["weights"], rtol=1e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("fixture,cfg", [("route_v3_sigmoid.npz", C.V3), ("route_v2lite_softmax.npz", C.V2_LITE)],
+                         ids=["v3", "v2-lite"])
+def test_topk_matches_transformers_gating(lib, fixture, cfg):
+    """FP32 logits routed by transformers' DeepSeek-V3 / V2 gating (make_route_pins.py) -> the same
+    expert sets; compared in ascending expert order because transformers leaves the top-k unsorted."""
+    g = np.load(GOLDEN / fixture)
+    bias = g["bias"] if "bias" in g.files else np.zeros(cfg.n_experts, np.float32)
+    idx, w = _topk_gpu(lib, cfg, g["logits"], bias)
+    order = np.argsort(idx, axis=-1, kind="stable")
+    assert np.array_equal(np.take_along_axis(idx, order, -1).astype(np.int64), g["indices"])
+    assert np.allclose(np.take_along_axis(w, order, -1), g["weights"], rtol=2e-6, atol=1e-7)
+
+
 def test_group_limited_ties_and_masking(lib, oracle):
     cfg = C.V3
     logits = np.zeros((4, cfg.n_experts), np.float32)       # all ties: lowest indices / groups win

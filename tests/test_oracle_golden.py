@@ -1,6 +1,7 @@
 """The CPU oracle against the reference's own golden vectors (tests/golden/, made by make_golden.py)
 and against independent restatements. CPU only."""
 import json
+import sys
 from pathlib import Path
 
 import numpy as np
@@ -155,3 +156,51 @@ def test_rmsnorm_matches_reference_rms(oracle):
     ref_b = g["out_bf16"].view(np.uint16)
     diff = np.abs(got_b.astype(np.int32) - ref_b.astype(np.int32))
     assert diff.max() <= 1 and (diff == 0).mean() > 0.99
+
+
+def _ascending(idx, w):
+    order = np.argsort(idx, axis=-1, kind="stable")
+    return np.take_along_axis(idx, order, -1).astype(np.int64), np.take_along_axis(w, order, -1)
+
+
+@pytest.mark.parametrize("fixture,name", [("route_v3_sigmoid.npz", "v3"), ("route_v2lite_softmax.npz", "v2-lite")])
+def test_published_gating_matches_transformers(oracle, fixture, name):
+    """Sigmoid group-limited (DeepSeek-V3) and softmax greedy (DeepSeek-V2-Lite) routing against the
+    transformers 5.5.0 gating functions (make_route_pins.py): same expert sets, weights to float32
+    rounding. The oracle orders each row by selection score, transformers leaves it unsorted, so both
+    are compared in ascending expert order."""
+    from eva_b200.config import CONFIGS
+    cfg = CONFIGS[name]
+    g = np.load(GOLDEN / fixture)
+    bias = g["bias"] if "bias" in g.files else np.zeros(cfg.n_experts, np.float32)
+    idx, w = _ascending(*oracle.route(g["logits"], bias, cfg))
+    assert np.array_equal(idx, g["indices"])
+    np.testing.assert_allclose(w, g["weights"], rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("name", ["v3", "v2-lite"])
+def test_published_gating_matches_transformers_live(oracle, name):
+    """The same comparison on 4096 fresh rows, calling transformers directly when it is installed."""
+    pytest.importorskip("transformers")
+    sys.path.insert(0, str(GOLDEN))
+    import make_route_pins as P
+    from eva_b200.config import CONFIGS
+    cfg = CONFIGS[name]
+    if name == "v3":
+        logits, bias = P.v3_inputs(4096, cfg.n_experts, seed=77)
+        ref_idx, ref_w = P.transformers_v3_route(logits, bias)
+    else:
+        logits, bias = P.v2lite_inputs(4096, cfg.n_experts, seed=78), np.zeros(cfg.n_experts, np.float32)
+        ref_idx, ref_w = P.transformers_v2lite_route(logits)
+    idx, w = _ascending(*oracle.route(logits, bias, cfg))
+    same = (idx == ref_idx).all(-1)
+    np.testing.assert_allclose(w[same], ref_w[same], rtol=2e-6, atol=1e-7)
+    # Rows whose expert sets differ must be ties: torch.topk breaks equal scores in no fixed order
+    # (the oracle takes the lower expert id), and torch's CPU sigmoid is not correctly rounded (the
+    # oracle's is), which moves a score by 1 ulp. The selection scores of both sets then agree.
+    choice = (oracle.scores(logits, cfg.router) + (bias if cfg.router != "softmax" else 0)).astype(np.float32)
+    diff = np.where(~same)[0]
+    assert len(diff) <= max(2, len(idx) // 1000)
+    for r in diff:
+        a, b = np.sort(choice[r, idx[r]]), np.sort(choice[r, ref_idx[r]])
+        np.testing.assert_allclose(a, b, rtol=3e-7, atol=0)
