@@ -326,10 +326,12 @@ int eo_moe_forward(const uint16_t* x, int x_is_f16, int M, int H, int I, int top
     uint16_t* wg = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) H * (I > sh_I ? I : sh_I));
     uint16_t* wu = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) H * (I > sh_I ? I : sh_I));
     uint16_t* wd = (uint16_t*) malloc(sizeof(uint16_t) * (size_t) H * (I > sh_I ? I : sh_I));
-    double* xs = (double*) malloc(sizeof(double) * (size_t) M * H);
-    double* ys = (double*) malloc(sizeof(double) * (size_t) M * H);
-    int* rows = (int*) malloc(sizeof(int) * M);
-    int* ks = (int*) malloc(sizeof(int) * M);
+    /* a row may select one expert in several slots: up to M * topk rows per expert */
+    const size_t R = (size_t) (M > 0 ? M : 1) * (topk > 0 ? topk : 1);
+    double* xs = (double*) malloc(sizeof(double) * R * H);
+    double* ys = (double*) malloc(sizeof(double) * R * H);
+    int* rows = (int*) malloc(sizeof(int) * R);
+    int* ks = (int*) malloc(sizeof(int) * R);
     int status = 0;
 
     /* per token, per slot contribution, summed in slot order: keep per-slot outputs */

@@ -6,11 +6,15 @@ module. The product (eva_b200) never imports it and has no CPU fallback.
 Restated from the reference (paths within Findddx/eva):
   * routers ........ sqrtsoftplus: runtime/ds41/model.py:404-416 (Block.route).
                      softmax (DeepSeek-V2-Lite) and sigmoid + bias, group-limited (DeepSeek-V3) are
-                     NOT in the reference; they follow the published DeepSeek gating and are
-                     "parity unpinned" against the reference.
+                     NOT in the reference; they follow the published DeepSeek gating, checked
+                     against transformers 5.5.0's DeepSeek-V2/V3 routing functions
+                     (tests/golden/make_route_pins.py).
   * run table ...... runtime/ds41/moe_coop2048.py:69-111 (reference_runs / reference_table),
                      generalised to any top-k / capacity.
   * EXL3 experts ... oracle/exl3_oracle.c (C restatement, see its header).
+  * CPU baseline ... oracle/cpu_fast.c: the same layer in float32 with dequantization fused into the
+                     GEMV, timed by bench.py as the CPU baseline (moe_forward_fast); checked against
+                     moe_forward, never used as the parity reference.
   * RMSNorm ........ runtime/ds41/model.py:968-970 rms(x, weight, eps) (mean square in FP32).
 
 Score functions are evaluated in float64 and rounded once to float32, so a GPU kernel that does
@@ -32,7 +36,8 @@ _lib = None
 
 
 def build(force: bool = False) -> Path:
-    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < (HERE / "exl3_oracle.c").stat().st_mtime:
+    srcs = [HERE / "exl3_oracle.c", HERE / "cpu_fast.c"]
+    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < max(f.stat().st_mtime for f in srcs):
         subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
     return LIB_PATH
 
@@ -63,6 +68,9 @@ def lib():
         L.eo_moe_forward.restype = i32
         L.eo_moe_forward.argtypes = [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, i32, i32,
                                      dbl, vp, vp, i32]
+        L.cf_moe_forward.restype = i32
+        L.cf_moe_forward.argtypes = [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, i32, vp, i32, i32,
+                                     dbl, vp, i32]
         _lib = L
     return _lib
 
@@ -281,6 +289,30 @@ def moe_forward(x_bits: np.ndarray, sel: np.ndarray, rw: np.ndarray, layer, thre
                               float(cfg.swiglu_limit), _ptr(out), None, int(threads))
     if st:
         raise RuntimeError(f"oracle moe_forward status {st}")
+    return out
+
+
+def moe_forward_fast(x_bits: np.ndarray, sel: np.ndarray, rw: np.ndarray, layer, threads: int = 0,
+                     with_shared: bool = True, x_is_f16: bool = False) -> np.ndarray:
+    """moe_forward in float32 with the dequantization fused into the GEMV (cpu_fast.c): the CPU
+    baseline bench.py times. Same arguments and result as moe_forward."""
+    cfg = layer.cfg
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    M, H = x.shape
+    sel32 = np.ascontiguousarray(sel, dtype=np.int32)
+    rw32 = np.ascontiguousarray(rw, dtype=np.float32)
+    assert str(layer.packed.device) == "cpu"
+    ptrs = np.ascontiguousarray(layer.packed.numpy().T, dtype=np.int64)   # [E, 9]
+    sh = None
+    if with_shared and layer.shared is not None:
+        sh = np.ascontiguousarray(layer.shared.numpy(), dtype=np.int64)
+    out = np.empty((M, H), dtype=np.float32)
+    st = lib().cf_moe_forward(_ptr(x), int(x_is_f16), M, H, cfg.inter, cfg.topk, ptrs.shape[0], _ptr(sel32),
+                              _ptr(rw32), _ptr(ptrs), cfg.bits, None if sh is None else _ptr(sh),
+                              cfg.shared_inter if sh is not None else 0, cfg.shared_bits,
+                              float(cfg.swiglu_limit), _ptr(out), int(threads))
+    if st:
+        raise RuntimeError(f"cpu_fast moe_forward status {st}")
     return out
 
 
