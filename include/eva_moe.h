@@ -173,7 +173,8 @@ int eva_exl3_dequant(const void* trellis, int32_t in_features, int32_t out_featu
  *   - All calls share the one array, which keeps the previous call's contents. Each call clears
  *     what must start at zero on its own stream. Calls that overlap on the GPU race on the array:
  *     issue them in order on one stream.
- *   - status_out (device int32, may be NULL) receives the call's EVA_STATUS_* bits.
+ *   - status_out (device int32, may be NULL) receives the call's EVA_STATUS_* bits; a call with M = 0
+ *     returns EVA_OK without touching the device and leaves *status_out as it was.
  * No cudaMalloc, cudaFree or other allocating routine is called. */
 int eva_moe_experts_noalloc(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
                             const void* sel, int32_t sel_is_i64, const float* rw,

@@ -148,3 +148,30 @@ def test_argument_errors_are_reported_without_a_gpu():
         _lib.EVA_ERR_WORKSPACE
     assert L.eva_moe_route(ctypes.byref(sh), fake, 1, 64, fake, None, None, fake, fake, None, n, None) == \
         _lib.EVA_ERR_INVALID
+
+
+def test_empty_batches_return_before_any_device_work():
+    """M = 0 is a valid call for every per-token entry point: arguments are checked, nothing is
+    launched (the library is called here with no GPU and never-dereferenced aligned addresses)."""
+    from eva_b200 import _lib
+    L = _lib.load()
+    sh = _lib.shape_of(C.V3)
+    a = 1 << 20                                   # 16-byte aligned, never dereferenced
+    tables = _lib.table_array([a] * 9)
+    shared = _lib.shared_array([a] * 9)
+    n = L.eva_moe_workspace_bytes(ctypes.byref(sh), 8)
+    ok = _lib.EVA_OK
+    assert L.eva_moe_topk(ctypes.byref(sh), a, 0, None, a, a, None) == ok
+    assert L.eva_moe_route(ctypes.byref(sh), a, 1, 0, a, None, None, a, a, a, n, None) == ok
+    for name in ("eva_moe_experts", "eva_moe_experts_decode", "eva_moe_experts_prefill"):
+        assert getattr(L, name)(ctypes.byref(sh), a, 1, 0, a, 1, a, tables, shared, a, n, a, None, None) == ok
+    assert L.eva_moe_experts_window(ctypes.byref(sh), a, 1, 0, a, 1, a, tables, shared, 0, 0, a, n, a, None,
+                                    None) == ok
+    assert L.eva_moe_forward(ctypes.byref(sh), a, 1, 0, a, None, tables, shared, a, n, None, a, None, None, None,
+                             None) == ok
+    assert L.eva_moe_experts_noalloc(ctypes.byref(sh), a, 1, 0, a, 1, a, tables, shared, None, a, None, None) == ok
+    assert L.eva_rmsnorm_residual(C.V3.hidden, 0, a, None, a, 1, 1e-6, a, None) == ok
+    # the same calls with a negative row count are argument errors
+    assert L.eva_moe_topk(ctypes.byref(sh), a, -1, None, a, a, None) == _lib.EVA_ERR_INVALID
+    assert L.eva_moe_experts(ctypes.byref(sh), a, 1, -1, a, 1, a, tables, shared, a, n, a, None, None) == \
+        _lib.EVA_ERR_INVALID
