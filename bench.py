@@ -77,6 +77,9 @@ def peaks():
     return 6650.0, "fallback"
 
 
+HBM_SPEC_GBS = 8000.0   # the north star's nominal B200 HBM3e figure; frac_of_spec is reported beside frac
+
+
 def tensor_peak():
     """Dense bf16 TFLOP/s for a kernel timed inside a long step (sustained figure)."""
     p = ROOT / "MEASURED_PEAKS.json"
@@ -466,6 +469,7 @@ def ep_bench(args, cfg, dev, rank, world, local):
                        "exchange": EXCHANGE[args.ep_transport],
                        "l2": "inputs larger than L2 (4.24 GB experts over the ranks, new routes every step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "frac_of_spec": achieved / HBM_SPEC_GBS,
                          "traffic": None, "peak_kind": peak_kind,
                          "kernel": "whole EP step per rank (bytes: this rank's selected experts + shared, "
                                    "max over ranks)",
@@ -825,6 +829,7 @@ def main():
                    "parallelism": "replicas" if world > 1 else "single",
                    "l2": "inputs larger than L2 (4.24 GB experts, different routes every step)"},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "frac_of_spec": achieved / HBM_SPEC_GBS,
                      "traffic": traffic, "peak_kind": peak_kind, "kernel": "eva_moe_experts (permute + experts_kernel)",
                      "alg_bytes_per_launch": statistics.mean(alg_bytes), "launch_ms": statistics.mean(exp_ms),
                      "distinct_experts_per_step": statistics.mean(U),
