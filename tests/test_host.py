@@ -175,3 +175,18 @@ def test_empty_batches_return_before_any_device_work():
     assert L.eva_moe_topk(ctypes.byref(sh), a, -1, None, a, a, None) == _lib.EVA_ERR_INVALID
     assert L.eva_moe_experts(ctypes.byref(sh), a, 1, -1, a, 1, a, tables, shared, a, n, a, None, None) == \
         _lib.EVA_ERR_INVALID
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the behaviour on a machine without CUDA")
+def test_operators_fail_loudly_without_cuda():
+    """No CPU fallback: every operator of the product refuses to run without a CUDA device."""
+    from eva_b200.ep import EPMoE, ExpertPlacement
+    from eva_b200.runner import EvaMoE, EvaMoERunner
+    cfg = C.MoEConfig("t", hidden=256, inter=128, n_experts=4, topk=2, router="softmax", bits=3)
+    layer = X.make_layer(cfg, "cpu", seed=0)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        EvaMoERunner("cpu", topk=2, hidden=256, inter=128, max_rows=4, n_experts=4)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        EvaMoE(layer)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        EPMoE(layer, ExpertPlacement.contiguous(cfg.n_experts, 1), max_tokens=4)
