@@ -30,6 +30,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -108,6 +109,11 @@ def zipf_bias(cfg, base, seed=3):
 # which the GPU clocks need a few steps to come back up)
 PREFILL_WARMUP = 5
 PREFILL_WARMUP_S = 0.3
+# the timed prefill region lasts at least this long (more steps than asked when they are short), so
+# that the GPU's power management has settled: tens of milliseconds after an idle or lighter phase
+# run at a higher clock than the sustained one
+PREFILL_TIMED_S = 1.0
+PREFILL_MAX_STEPS = 400
 
 
 def prefill_measure(cfg, layer, dev, steps, warmup, M):
@@ -152,14 +158,23 @@ def prefill_measure(cfg, layer, dev, steps, warmup, M):
         if i >= warmup:
             torch.cuda.synchronize()
     torch.cuda.synchronize()
+    per_step = (time.perf_counter() - t_w) / i
+    steps = max(steps, min(PREFILL_MAX_STEPS, math.ceil(PREFILL_TIMED_S / max(per_step, 1e-6))))
     loads = np.bincount(idx.cpu().numpy().ravel(), minlength=cfg.n_experts)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(dev.index if dev.index is not None else 0).__enter__()
+    clocks.wait_first()
+    c_start = clocks.mark()
     t0.record()
     for i in range(steps):
         step(i, evs[i])
     t1.record()
     torch.cuda.synchronize()
+    time.sleep(0.06)   # let the sampler report the end of the region
+    c_end = clocks.mark()
+    clocks.__exit__(None, None, None)
+    clock_summary = clocks.summary(c_start, c_end)
     ms = t0.elapsed_time(t1) / steps
     ems = statistics.mean(a.elapsed_time(b) for a, b in evs)
     flop_exp = 6.0 * cfg.hidden * (M * cfg.topk * cfg.inter + M * cfg.shared_inter)
@@ -178,7 +193,8 @@ def prefill_measure(cfg, layer, dev, steps, warmup, M):
                          "frac": (flop_exp) / (ems * 1e-3) / 1e12 / peak, "peak_kind": kind,
                          "kernel": "eva_moe_experts_prefill (permute + rotate + gate/up + down + combine)",
                          "alg_flop_per_launch": flop_exp, "launch_ms": ems},
-            "step_tflops_incl_router": (flop_exp + flop_router) / (ms * 1e-3) / 1e12}
+            "step_tflops_incl_router": (flop_exp + flop_router) / (ms * 1e-3) / 1e12,
+            "clocks": clock_summary}
 
 
 class ClockSampler:
