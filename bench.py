@@ -151,14 +151,20 @@ def prefill_measure(cfg, layer, dev, steps, warmup, M):
 
     # at least `warmup` untimed steps and at least PREFILL_WARMUP_S seconds of them
     t_w = time.perf_counter()
-    i = 0
+    i, t_mid = 0, None
     while i < warmup or time.perf_counter() - t_w < PREFILL_WARMUP_S:
         step(i)
         i += 1
         if i >= warmup:
             torch.cuda.synchronize()
+            if t_mid is None:
+                t_mid = (time.perf_counter(), i)   # the steady part starts after the first `warmup` steps
     torch.cuda.synchronize()
-    per_step = (time.perf_counter() - t_w) / i
+    t_now = time.perf_counter()
+    if t_mid is not None and i > t_mid[1]:
+        per_step = (t_now - t_mid[0]) / (i - t_mid[1])
+    else:
+        per_step = (t_now - t_w) / max(i, 1)
     steps = max(steps, min(PREFILL_MAX_STEPS, math.ceil(PREFILL_TIMED_S / max(per_step, 1e-6))))
     loads = np.bincount(idx.cpu().numpy().ravel(), minlength=cfg.n_experts)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
