@@ -16,7 +16,9 @@ Format (writer tools/pack_exl3.py:13-17,77-112,188-199; reader runtime/ds41/cach
 The reference writer starts the records right after the index; this writer starts them at the next
 4096-byte boundary (the index gives every record's offset, so readers are unaffected, and every
 record is then 4096-aligned for O_DIRECT reads). The reference reader accepts only 384 experts per
-layer (its N_EXPERTS, cache.py:42); the format itself has no such limit.
+layer (its N_EXPERTS, cache.py:42); the format itself has no such limit. tests/golden/
+make_pack_pin.py runs the reference writer on seeded experts: its header, index fields (record
+offsets aside) and record bytes equal this writer's.
 """
 from __future__ import annotations
 

@@ -72,3 +72,25 @@ def test_expert_subset_and_shape_checks(packed, tmp_path):
     bad.write_bytes(b"NOTAPACK" + bytes(64))
     with pytest.raises(ValueError):
         Pack.open(str(bad))
+
+
+def test_pack_matches_the_reference_packer(tmp_path):
+    """The reference's own tools/pack_exl3.py, run on the same seeded experts (make_pack_pin.py),
+    wrote the same header, the same index fields apart from the record offset, and the same record
+    bytes as write_pack."""
+    import hashlib
+    import json
+    from pathlib import Path
+    pin = json.loads((Path(__file__).resolve().parent / "golden" / "pack_ref_pin.json").read_text())
+    cfg = C.MoEConfig(**pin["config"])
+    layers = [make_layer(cfg, "cpu", seed=s) for s in pin["seeds"]]
+    path = tmp_path / "experts.bin"
+    write_pack(str(path), layers)
+    raw = path.read_bytes()
+    assert raw[:8].decode() == pin["magic"]
+    assert list(struct.unpack("<IIII", raw[8:24])) == pin["header"]
+    pack = Pack.open(str(path))
+    for i, (ref_slot, ref_sha) in enumerate(zip(pin["slots"], pin["record_sha256"])):
+        ours = pack.slots[i]
+        assert list(ours[1:]) == ref_slot[1:]
+        assert hashlib.sha256(raw[ours[0]: ours[0] + ours[1]]).hexdigest() == ref_sha
