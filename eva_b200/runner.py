@@ -59,6 +59,9 @@ class EvaMoERunner:
             raise ValueError("max_rows must be a positive int")
         self.topk, self.hidden, self.inter, self.max_rows, self.n_experts = topk, hidden, inter, max_rows, n_experts
         self._lock, self._failed = threading.Lock(), False
+        # like the reference runner (moe_coop2048.py:263-290): one owner thread, the construction stream
+        self._owner_thread = threading.get_ident()
+        self._owner_stream = torch.cuda.current_stream(self.device).cuda_stream
         self._ws = {}
         self.out = torch.empty(max_rows, hidden, device=self.device, dtype=_F32)
         self.rw = torch.empty(max_rows, topk, device=self.device, dtype=_F32)
@@ -95,6 +98,17 @@ class EvaMoERunner:
         return packed, n_local
 
     def run(self, x, sel, weights, packed, k, limit, *, check_bounds=True):
+        """Routed experts of `rows` tokens: float32 [rows, hidden], an owned tensor.
+
+        Same arguments and errors as the reference runner's run (moe_coop2048.py:255-305): ValueError
+        for bad arguments; RuntimeError from another thread, on another stream than the construction
+        stream, under graph capture, or while a call is in progress; any error after the arguments
+        were accepted poisons the runner. check_bounds=True reads the device status word back (the
+        reference's mandatory bounds check); False skips that host read (the kernels still skip and
+        flag an out-of-range expert), which the reference does not offer.
+        """
+        if threading.get_ident() != self._owner_thread:
+            raise RuntimeError("EvaMoERunner requires its owner thread")
         if self._failed:
             raise RuntimeError("EvaMoERunner launch failed earlier; discard this runner")
         if type(k) not in (int, float) or k not in (2, 3, 4):
@@ -114,6 +128,10 @@ class EvaMoERunner:
         tables, n_local = self._tables(packed)
         for name, t in (("x", x), ("sel", sel), ("weights", weights), *(("packed", t) for t in tables)):
             _require_cuda(t, self.device, name)
+        if torch.cuda.current_stream(self.device).cuda_stream != self._owner_stream:
+            raise RuntimeError("EvaMoERunner requires its construction stream")
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("EvaMoERunner does not support graph capture")
         if not self._lock.acquire(blocking=False):
             raise RuntimeError("EvaMoERunner is already in use")
         try:
@@ -139,7 +157,7 @@ class EvaMoERunner:
                 if st.value:
                     raise RuntimeError(f"device status {st.value:#x}")
             return out.clone()
-        except RuntimeError:
+        except BaseException:
             self._failed = True
             raise
         finally:

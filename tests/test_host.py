@@ -190,3 +190,20 @@ def test_operators_fail_loudly_without_cuda():
         EvaMoE(layer)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         EPMoE(layer, ExpertPlacement.contiguous(cfg.n_experts, 1), max_tokens=4)
+
+
+def test_runner_owner_thread_and_poisoning_checks_come_first():
+    """EvaMoERunner.run refuses calls from a thread other than its owner and from a poisoned runner
+    before looking at its arguments, as the reference runner does (moe_coop2048.py:263-266)."""
+    import threading
+    from eva_b200.runner import EvaMoERunner
+    r = EvaMoERunner.__new__(EvaMoERunner)      # no CUDA here: only the host-side checks run
+    r._owner_thread, r._failed = threading.get_ident() + 1, False
+    with pytest.raises(RuntimeError, match="owner thread"):
+        r.run(None, None, None, None, 3, 0.0)
+    r._owner_thread, r._failed = threading.get_ident(), True
+    with pytest.raises(RuntimeError, match="discard"):
+        r.run(None, None, None, None, 3, 0.0)
+    r._failed = False
+    with pytest.raises(ValueError, match="K must be"):
+        r.run(None, None, None, None, 5, 0.0)
