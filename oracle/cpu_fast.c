@@ -30,7 +30,8 @@ uint16_t eo_f16_from_double(double v);
 
 static float cf_cb[65536];   /* trellis state -> codebook value */
 static float cf_f16[65536];  /* fp16 bits -> float */
-static uint8_t cf_w0[5][256], cf_w1[5][256], cf_sh[5][256];   /* window words and shift, K = 2..4 */
+static uint8_t cf_lw0[5][32], cf_lw1[5][32], cf_loff[5][32];  /* per group of 8 positions: its two words
+                                                                 * and the bit offset of its first window */
 static uint8_t cf_dst[256];  /* position p -> k * 16 + n inside the tile */
 static int cf_ready;
 
@@ -39,14 +40,16 @@ static void cf_init(void)
     if (cf_ready) return;
     for (uint32_t s = 0; s < 65536; ++s) cf_f16[s] = (float) eo_f16_to_double((uint16_t) s);
     for (uint32_t s = 0; s < 65536; ++s) cf_cb[s] = cf_f16[eo_mul1_decode(s)];
+    /* positions 8l .. 8l+7 end at bits (8l + j + 1) K: their windows span 16 + 7K bits starting at
+     * bit (8l + 1) K - 16 (circular), which lie inside two consecutive words for K <= 4 */
     for (int K = 2; K <= 4; ++K) {
         const int nbits = 256 * K, words = 8 * K;
-        for (int p = 0; p < 256; ++p) {
-            int start = (p + 1) * K - 16;
+        for (int l = 0; l < 32; ++l) {
+            int start = (8 * l + 1) * K - 16;
             if (start < 0) start += nbits;
-            cf_w0[K][p] = (uint8_t) (start >> 5);
-            cf_w1[K][p] = (uint8_t) (((start >> 5) + 1) % words);
-            cf_sh[K][p] = (uint8_t) (48 - (start & 31));
+            cf_lw0[K][l] = (uint8_t) (start >> 5);
+            cf_lw1[K][l] = (uint8_t) (((start >> 5) + 1) % words);
+            cf_loff[K][l] = (uint8_t) (start & 31);
         }
     }
     for (int p = 0; p < 256; ++p) {
@@ -89,12 +92,15 @@ static void cf_tile_fma(const float* wt, const float* x, int ldx, int n, float* 
     }
 }
 
-/* The 256 codebook values of one tile, stored at wt[k * 16 + n]. */
-static inline void cf_decode_tile(const uint32_t* t, const uint8_t* w0, const uint8_t* w1, const uint8_t* sh, float* wt)
+/* The 256 codebook values of one K-bit tile, stored at wt[k * 16 + n]. */
+static inline void cf_decode_tile(const uint32_t* t, int K, float* wt)
 {
-    for (int p = 0; p < 256; ++p) {
-        const uint64_t v = ((uint64_t) t[w0[p]] << 32) | t[w1[p]];
-        wt[cf_dst[p]] = cf_cb[(uint32_t) (v >> sh[p]) & 0xffffu];
+    const uint8_t *w0 = cf_lw0[K], *w1 = cf_lw1[K], *off = cf_loff[K];
+    for (int l = 0; l < 32; ++l) {
+        const uint64_t v = ((uint64_t) t[w0[l]] << 32) | t[w1[l]];
+        const int top = 48 - off[l];
+        const uint8_t* dst = cf_dst + 8 * l;
+        for (int j = 0; j < 8; ++j) wt[dst[j]] = cf_cb[(uint32_t) (v >> (top - j * K)) & 0xffffu];
     }
 }
 
@@ -102,7 +108,6 @@ static inline void cf_decode_tile(const uint32_t* t, const uint8_t* w0, const ui
 static void cf_gemv(const uint32_t* trellis, int in, int out, int K, const float* x, int n, float* y)
 {
     const int kt_n = in / 16, nt_n = out / 16, words = 8 * K;
-    const uint8_t *w0 = cf_w0[K], *w1 = cf_w1[K], *sh = cf_sh[K];
     #pragma omp parallel for schedule(static)
     for (int nt = 0; nt < nt_n; ++nt) {
         float wt[256], acc[CF_ROWS * 16];
@@ -110,7 +115,7 @@ static void cf_gemv(const uint32_t* trellis, int in, int out, int K, const float
             const int nr = n - r0 < CF_ROWS ? n - r0 : CF_ROWS;
             memset(acc, 0, sizeof(float) * 16 * nr);
             for (int kt = 0; kt < kt_n; ++kt) {
-                cf_decode_tile(trellis + ((size_t) kt * nt_n + nt) * words, w0, w1, sh, wt);
+                cf_decode_tile(trellis + ((size_t) kt * nt_n + nt) * words, K, wt);
                 cf_tile_fma(wt, x + (size_t) r0 * in + kt * 16, in, nr, acc);
             }
             for (int r = 0; r < nr; ++r) memcpy(y + (size_t) (r0 + r) * out + nt * 16, acc + r * 16, 64);
