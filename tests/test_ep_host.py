@@ -129,3 +129,51 @@ def test_expert_subset_holds_the_same_records():
     assert part.packed.shape == (9, 3) and part.n_local == 3
     with pytest.raises(ValueError):
         make_layer(SMALL, "cpu", experts=(1, 1))
+
+
+def _dropout_worker(rank, world, port, outdir):
+    """Rank 1 joins the group but never enters the step; rank 0's step must end with an error
+    within the process group's timeout instead of waiting for it."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import time
+    import torch.distributed as dist
+    from datetime import timedelta
+    from eva_b200.ep import EPMoE
+    from eva_b200.experts import make_layer
+    from oracle.ep_oracle import OracleEpOps
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    pl = ExpertPlacement.contiguous(SMALL.n_experts, world)
+    layer = make_layer(SMALL, "cpu", seed=5, experts=pl.experts_of(rank))
+    ep = EPMoE(layer, pl, max_tokens=4, mode="exact", ops=OracleEpOps(layer, pl))   # both ranks set up
+    if rank == 1:
+        time.sleep(8)                  # leaves between steps: past rank 0's timeout, no collective
+        return
+    x = torch.randn(4, SMALL.hidden, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
+    t0 = time.time()
+    try:
+        ep.forward(x, out_f32=torch.empty(4, SMALL.hidden))
+        outcome = "completed"
+    except Exception as e:             # the collective's timeout surfaces as an exception on the host
+        outcome = f"raised {type(e).__name__}"
+    with open(os.path.join(outdir, "rank0.txt"), "w") as f:
+        f.write(f"{outcome}\n{time.time() - t0:.1f}\n")
+
+
+def test_ep_step_fails_on_the_host_when_a_rank_never_joins():
+    import time
+    with tempfile.TemporaryDirectory() as d:
+        ctx = mp.start_processes(_dropout_worker, args=(2, _free_port(), d), nprocs=2, start_method="spawn",
+                                 join=False)
+        t_end = time.time() + 120
+        done = False
+        while not done and time.time() < t_end:
+            done = ctx.join(timeout=1)
+        if not done:
+            for p in ctx.processes:
+                if p.is_alive():
+                    p.kill()
+            pytest.fail("workers did not finish")
+        outcome, took = open(os.path.join(d, "rank0.txt")).read().splitlines()[:2]
+        assert outcome.startswith("raised"), outcome
+        assert float(took) < 30.0
