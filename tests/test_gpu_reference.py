@@ -207,3 +207,61 @@ def test_prefill_speed_vs_reference_kernels(ref, capsys):
               f"({M // chunk} calls of {chunk} tokens), eva {times['eva']:.3f} ms, speed-up "
               f"{times['reference'] / times['eva']:.2f}x; eva vs reference max-rel-err {err:.2e}, cosine {cos:.7f}")
     assert err <= 2e-2 and cos >= 0.9999
+
+
+def test_shared_expert_matches_reference_kernels(ref, oracle):
+    """The shared expert's three EXL3 linears (exllamav3 LinearEXL3 in the reference, runtime/ds41/
+    exl3_linear.py:135-151, not installed here) checked through the reference's own coop kernels, which
+    run the same EXL3 linear: a table whose 6 columns all hold the DeepSeek-V3 shared expert, every token
+    routed to all 6 with weight 1, gives 6 x the shared expert's output (swiglu limit 0, where the two
+    activation clamp orders agree). Ours: eva_moe_experts with every routed slot inactive and the shared
+    expert on (its virtual-slot path)."""
+    cfg = C.V3.with_(n_experts=6, topk=6, n_group=1, topk_group=1)
+    layer_d = make_layer(cfg, DEV, seed=4, n_fill=0)      # routed records unused; the shared one is filled
+    M, H, I, K = 5, cfg.hidden, cfg.shared_inter, cfg.shared_bits
+    x16 = torch.randn(M, H, generator=torch.Generator().manual_seed(7)).to(torch.float16).to(DEV)
+    sel = torch.arange(6, device=DEV, dtype=torch.int64).repeat(M, 1)
+    # the reference: 6 identical columns pointing at the shared expert's tensors
+    cols = [torch.full((6,), int(a), dtype=torch.int64, device=DEV) for a in layer_d.shared.tolist()]
+    slots = M * 6
+    o = dict(device=DEV)
+    had_g = torch.empty(slots, H, dtype=torch.float16, **o)
+    had_u = torch.empty_like(had_g)
+    gu_g = torch.empty(slots, I, dtype=torch.float16, **o)
+    gu_u = torch.empty_like(gu_g)
+    act = torch.empty_like(gu_g)
+    d_out = torch.empty(slots, H, dtype=torch.float32, **o)
+    ctr = torch.zeros(ref.ref_coop_ctr_len(M, 6, I, H), dtype=torch.int32, **o)
+    out = torch.empty(M, H, dtype=torch.float32, **o)
+    tabs = (ctypes.c_void_p * 9)(*[t.data_ptr() for t in cols])
+    rw16 = torch.ones(M, 6, device=DEV).half()
+    assert ref.ref_coop_run(x16.data_ptr(), sel.data_ptr(), rw16.data_ptr(), M, 6, H, I, tabs, 6, had_g.data_ptr(),
+                            had_u.data_ptr(), gu_g.data_ptr(), gu_u.data_ptr(), act.data_ptr(), d_out.data_ptr(),
+                            ctr.data_ptr(), M, out.data_ptr(), K, 0.0, stream()) == 0
+    y_ref = (out / 6).cpu().numpy()
+    # ours: shared expert only
+    lib = _lib.load()
+    sh = _lib.shape_of(cfg)
+    ws = torch.zeros(lib.eva_moe_workspace_bytes(ctypes.byref(sh), M), dtype=torch.uint8, device=DEV)
+    y = torch.full((M, H), float("nan"), device=DEV)
+    rw0 = torch.zeros(M, 6, device=DEV)
+    _lib.check(lib.eva_moe_experts(ctypes.byref(sh), x16.data_ptr(), 0, M, sel.data_ptr(), 1, rw0.data_ptr(),
+                                   _lib.table_array(tuple(layer_d.packed.unbind(0))),
+                                   _lib.shared_array(layer_d.shared.tolist()), ws.data_ptr(), ws.numel(), y.data_ptr(),
+                                   None, stream()), "experts")
+    st = ctypes.c_int32(0)
+    _lib.check(lib.eva_moe_read_status(ws.data_ptr(), ctypes.byref(st), stream()), "status")
+    assert st.value == 0
+    y_eva = y.cpu().numpy()
+    host = layer_d.host_copy()
+    ref64 = oracle.moe_forward(x16.cpu().view(torch.int16).numpy().view(np.uint16), sel.cpu().numpy(),
+                               rw0.cpu().numpy(), host, with_shared=True, x_is_f16=True)
+    scale = np.abs(ref64).max()
+    e_ref = np.abs(y_ref - ref64).max() / scale
+    e_eva = np.abs(y_eva - ref64).max() / scale
+    e_cross = np.abs(y_eva - y_ref).max() / scale
+    cos = float((y_eva.ravel() @ y_ref.ravel()) / (np.linalg.norm(y_eva) * np.linalg.norm(y_ref)))
+    print(f"V3 shared expert M={M}: ref-vs-oracle {e_ref:.2e}, eva-vs-oracle {e_eva:.2e}, eva-vs-ref {e_cross:.2e}, "
+          f"cos {cos:.7f}")
+    assert e_cross <= 2e-2 and cos >= 0.9999
+    assert e_eva <= 3e-3
