@@ -105,6 +105,10 @@ def zipf_bias(cfg, base, seed=3):
     return (base + off).contiguous()
 
 
+# decode: identical steps for at least this long right before the timed ones (clock sampling window)
+DECODE_SETTLE_S = 1.0
+DECODE_SETTLE_MAX = 20000
+
 # untimed prefill steps before the timed ones (the leg can follow seconds of CPU-only work, after
 # which the GPU clocks need a few steps to come back up)
 PREFILL_WARMUP = 5
@@ -297,12 +301,9 @@ def run_reference(args):
     from eva_b200.experts import make_layer
     cfg = CONFIGS[args.config]
     threads = host_threads()
-    # generating all 256 experts on the host would take minutes at 4 GB, so every expert shares one of
-    # 8 distinct records (same bytes per expert, same arithmetic; the CPU path is bound by decode
-    # arithmetic, not by memory traffic)
-    layer = make_layer(cfg, "cpu", seed=0, n_fill=8)
-    from eva_b200.experts import replicate_experts
-    replicate_experts(layer, 8)
+    # every expert its own seeded record (the same bytes as the GPU arm's layer), 4.24 GB for V3
+    torch.set_num_threads(threads)
+    layer = make_layer(cfg, "cpu", seed=0)
     M = args.batch
     g = torch.Generator().manual_seed(1)
     xs = torch.randn(args.steps + args.warmup, M, cfg.hidden, generator=g).to(torch.bfloat16)
@@ -319,8 +320,10 @@ def run_reference(args):
         tokens += n
     total = sum(times)
     value = tokens / total
-    sample = (f"{rows} of the {M} tokens of each step's batch (FP32 router, top-{cfg.topk} routed experts + shared "
-              f"expert in float32 with fused EXL3 dequantization, {threads} threads), on rank 0's host cores")
+    sample = (f"{rows} of the {M} tokens of each step's batch through this repository's float32 C port of the "
+              f"path (oracle/cpu_fast.c: FP32 router, top-{cfg.topk} routed experts + shared expert, EXL3 "
+              f"dequantization fused into the GEMV, {threads} threads) over {cfg.n_experts} distinct expert records, "
+              f"on rank 0's host cores; the reference's own CPU expert path needs exllamav3, which is not installed")
     world = args.gpus
     # the eva arm's config for the same run (bench.py decode line), the sample described in cpu_baseline
     config = {"workload": f"DeepSeek-{cfg.name.upper()} MoE layer decode (EXL3 K{cfg.bits}), batch {M} tokens/step"
@@ -743,13 +746,28 @@ def main():
     if world > 1:
         dist.barrier()
 
+    # settle: identical steps (cycling over the batches) for at least DECODE_SETTLE_S right before
+    # the timed steps, so that the clocks sampled over settle + timed steps describe the timed
+    # region (K steps of < 1 ms each are shorter than the sampler's period); timed on their own as
+    # the sustained figure
+    c_start = clocks.mark()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    settle_steps, w_settle = 0, time.perf_counter()
+    s0.record(stream)
+    while time.perf_counter() - w_settle < DECODE_SETTLE_S and settle_steps < DECODE_SETTLE_MAX:
+        step(settle_steps % nb)
+        settle_steps += 1
+        if settle_steps % 64 == 0:
+            torch.cuda.synchronize()   # keep the host from running far ahead of the device
+    s1.record(stream)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    settle_ms = s0.elapsed_time(s1)
     if world > 1:
         dist.barrier()
-    c_start = clocks.mark()
+    c_timed = clocks.mark()
     t0.record(stream)
     for i in range(steps):
         step(warmup + i, evs[i])
@@ -795,9 +813,9 @@ def main():
 
     clocks.__exit__(None, None, None)
     clock_summary = clocks.summary(c_start, c_end)
-    if not clock_summary["samples"]:
-        clock_summary = dict(clocks.summary(), note="timed region shorter than the 50 ms sampling period; "
-                                                    "samples from warm-up through e2e")
+    clock_summary["window"] = (f"{settle_steps} identical untimed steps ({settle_ms:.0f} ms, no gap) immediately "
+                               f"before the {steps} timed steps, and the timed steps; "
+                               f"{clocks.summary(c_timed, c_end)['samples']} samples inside the timed steps alone")
 
     # ---- roofline of the fused experts launch -------------------------------------------------
     U = [len(np.unique(idx_host[warmup + i])) for i in range(steps)]
@@ -822,9 +840,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        from eva_b200.experts import replicate_experts
-        host = make_layer(cfg, "cpu", seed=0, n_fill=8)
-        replicate_experts(host, 8)
+        # the device layer's own records in host memory: every expert distinct, the same 4.24 GB
+        host = layer.host_copy()
         xb = xs[:min(nb, 8)].cpu().view(torch.int16).numpy().view(np.uint16)
         threads = host_threads()
         cpu_sample(cfg, host, xb[0], threads)   # warm-up
@@ -835,8 +852,11 @@ def main():
             ts.append(dt)
             n_tok += n
         cpu = {"value": n_tok / sum(ts), "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{len(ts)} whole batch-{M} steps of this run's inputs (FP32 router, top-{cfg.topk} routed "
-                         f"experts + shared expert in float32 with fused EXL3 dequantization, oracle/cpu_fast.c)"}
+               "sample": f"{len(ts)} whole batch-{M} steps of this run's inputs through this repository's float32 C "
+                         f"port of the path (oracle/cpu_fast.c: FP32 router, top-{cfg.topk} routed experts + shared "
+                         f"expert with the EXL3 dequantization fused into the GEMV), over the same "
+                         f"{cfg.n_experts} distinct expert records as the GPU run; not the reference's own code, "
+                         f"whose CPU expert path needs exllamav3 (not installed)"}
 
     tokens = M * steps * world
     line = {
@@ -861,6 +881,9 @@ def main():
                 "d2h_bytes_per_step": M * cfg.hidden * 2},
         "gpu_launches": 4 * steps,
         "clocks": clock_summary,
+        "sustained": {"value": M * settle_steps / (settle_ms * 1e-3), "unit": UNIT, "steps": settle_steps,
+                      "ms_per_step": settle_ms / max(settle_steps, 1),
+                      "note": "the settle steps before the timed region, timed as one block (>= 1 s)"},
         "device_status": st,
         "prefill": prefill,
     }

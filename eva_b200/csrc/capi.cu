@@ -10,7 +10,7 @@ namespace eva {
 
 static size_t up256(size_t n) { return (n + 255) & ~static_cast<size_t>(255); }
 
-WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split, bool routing)
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split, bool routing, bool tensor_core)
 {
     WsLayout L{};
     L.max_rows = max_rows;
@@ -50,9 +50,9 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split, bool ro
     L.asum = take(St * L.nchA * 4);
     L.tstart = take((E + 2) * 4);
     L.pscan = take(permute_scratch_ints(max_rows, static_cast<int>(E)) * 4);
-    L.pxg = take(St * H * 2);
-    L.pxu = take(St * H * 2);
-    L.pap = take(St * L.imax * 2);
+    L.pxg = take(tensor_core ? St * H * 2 : 0);
+    L.pxu = take(tensor_core ? St * H * 2 : 0);
+    L.pap = take(tensor_core ? St * L.imax * 2 : 0);
     const size_t pa = allow_split ? std::min<size_t>(PARTA_ITEMS, R * L.nchA * 4) : 0;
     L.partA = take(pa * 2 * RUN_ROWS * 128 * 4);
     L.max_split = allow_split ? 4 : 1;
@@ -228,6 +228,21 @@ int eva_moe_permute_ws(const EvaMoeShape* shape, const void* sel, int32_t sel_is
 
 namespace eva {
 
+int experts_validate(const EvaMoeShape* shape, const void* x, int32_t M, const void* sel, const float* rw,
+                     const int64_t* const* tables, const int64_t* shared, const float* out_f32, const void* out_bf16)
+{
+    if (!shape_ok(shape) || M < 0 || !x || !sel || !rw || !tables) return EVA_ERR_INVALID;
+    if (!out_f32 && !out_bf16) return EVA_ERR_INVALID;
+    if (shape->shared_inter && !shared) return EVA_ERR_INVALID;
+    if (!aligned(x, 8) || !aligned(out_f32, 16) || !aligned(out_bf16, 8)) return EVA_ERR_INVALID;
+    for (int i = 0; i < 9; ++i)
+        if (!tables[i] || !aligned(tables[i], 8)) return EVA_ERR_INVALID;
+    if (shape->shared_inter)
+        for (int i = 0; i < 9; ++i)
+            if (shared[i] == 0 || (shared[i] & 15)) return EVA_ERR_INVALID;   // bulk copies need 16 B
+    return EVA_OK;
+}
+
 int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
                  int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
                  void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,
@@ -238,17 +253,11 @@ int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int
         shared_rows = M;
     }
     if (shared_row0 < 0 || shared_row0 + shared_rows > M) return EVA_ERR_INVALID;
-    if (!shape_ok(shape) || M < 0 || !x || !sel || !rw || !tables || !workspace) return EVA_ERR_INVALID;
-    if (!out_f32 && !out_bf16) return EVA_ERR_INVALID;
-    if (shape->shared_inter && !shared) return EVA_ERR_INVALID;
-    if (!aligned(x, 8) || !aligned(out_f32, 16) || !aligned(out_bf16, 8)) return EVA_ERR_INVALID;
-    for (int i = 0; i < 9; ++i)
-        if (!tables[i] || !aligned(tables[i], 8)) return EVA_ERR_INVALID;
-    if (shape->shared_inter)
-        for (int i = 0; i < 9; ++i)
-            if (shared[i] == 0 || (shared[i] & 15)) return EVA_ERR_INVALID;   // bulk copies need 16 B
+    if (!workspace) return EVA_ERR_INVALID;
+    const int v = experts_validate(shape, x, M, sel, rw, tables, shared, out_f32, out_bf16);
+    if (v != EVA_OK) return v;
     if (M == 0) return EVA_OK;
-    const WsLayout L = ws_layout(*shape, M, allow_split, /*routing=*/false);
+    const WsLayout L = ws_layout(*shape, M, allow_split, /*routing=*/false, /*tensor_core=*/path != 1);
     if (workspace_bytes < L.total) return EVA_ERR_WORKSPACE;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     PermuteArgs pa;

@@ -27,8 +27,10 @@ struct WsLayout {
 
 // allow_split = false leaves out the split-k partial buffer (gate/up items are then never split);
 // routing = false leaves out the router's regions (weight split planes, slice partial logits), which
-// come last, so every other offset is the same either way.
-WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split = true, bool routing = true);
+// come last, so every other offset is the same either way. tensor_core = false leaves out the
+// tensor-core path's sorted input copies (pxg, pxu, pap) for calls that always take the decode kernel.
+WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split = true, bool routing = true,
+                   bool tensor_core = true);
 
 // Counter block layout inside `counters` (int32 indices).
 struct CtrLayout {
@@ -99,7 +101,14 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream);
 constexpr int PREFILL_MIN_ROWS = 129;   // eva_moe_experts takes the tensor-core path from this many rows
 constexpr int PF_TILE_ROWS = 256;       // rows of one expert per tensor-core CTA (two 128-row MMA halves)
 
-// Permutation + fused experts on a caller-provided workspace laid out by ws_layout(shape, M, allow_split).
+// Argument checks of the fused expert entry points (pointers, alignment, shared-expert tables):
+// EVA_OK or EVA_ERR_INVALID; no device work.
+int experts_validate(const EvaMoeShape* shape, const void* x, int32_t M, const void* sel, const float* rw,
+                     const int64_t* const* tables, const int64_t* shared, const float* out_f32, const void* out_bf16);
+
+// Permutation + fused experts on a caller-provided workspace laid out by
+// ws_layout(shape, M, allow_split, false, path != 1): path 1 (decode kernel only) needs no
+// tensor-core buffers.
 int experts_impl(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M, const void* sel,
                  int32_t sel_is_i64, const float* rw, const int64_t* const* tables, const int64_t* shared,
                  void* workspace, size_t workspace_bytes, float* out_f32, void* out_bf16, cudaStream_t st,

@@ -53,8 +53,12 @@ extern "C" int eva_moe_experts_noalloc(const EvaMoeShape* shape, const void* x, 
     if (!shape || M < 0) return EVA_ERR_INVALID;
     if (eva_moe_workspace_bytes(shape, 1) == 0) return EVA_ERR_INVALID;
     if (M == 0) return EVA_OK;
-    const WsLayout L = ws_layout(*shape, M, /*allow_split=*/false, /*routing=*/false);
+    // every call takes the decode kernel (path 1), so the layout holds no tensor-core buffers
+    const WsLayout L = ws_layout(*shape, M, /*allow_split=*/false, /*routing=*/false, /*tensor_core=*/false);
     if (L.total > EVA_NOALLOC_SCRATCH_BYTES) return EVA_ERR_WORKSPACE;   // too many rows for the fixed scratch
+    // all argument checks before any device call (symbol lookup, memset, launches)
+    const int v = experts_validate(shape, x, M, sel, rw, tables, shared, out_f32, out_bf16);
+    if (v != EVA_OK) return v;
     void* base = nullptr;
     if (scratch_address(&base) != cudaSuccess) return EVA_ERR_CUDA;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -62,7 +66,7 @@ extern "C" int eva_moe_experts_noalloc(const EvaMoeShape* shape, const void* x, 
     // permutation kernel of this call
     if (cudaMemsetAsync(static_cast<unsigned char*>(base) + L.status, 0, 4, st) != cudaSuccess) return EVA_ERR_CUDA;
     const int rc = experts_impl(shape, x, x_is_bf16, M, sel, sel_is_i64, rw, tables, shared, base, L.total, out_f32,
-                                out_bf16, st, /*allow_split=*/false);
+                                out_bf16, st, /*allow_split=*/false, /*path=*/1);
     if (rc != EVA_OK) return rc;
     if (status_out &&
         cudaMemcpyAsync(status_out, static_cast<unsigned char*>(base) + L.status, 4, cudaMemcpyDeviceToDevice, st) !=

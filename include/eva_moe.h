@@ -167,7 +167,10 @@ int eva_exl3_dequant(const void* trellis, int32_t in_features, int32_t out_featu
  * cudaMalloc because it can synchronise the device. The caller passes inputs and outputs exactly as
  * for eva_moe_experts; the scratch is a file-scope device array of EVA_NOALLOC_SCRATCH_BYTES.
  *   - Calls whose scratch would exceed that size are rejected with EVA_ERR_WORKSPACE (for the
- *     DeepSeek-V3 shape this allows up to 29 tokens per call, DeepSeek-V2-Lite 108).
+ *     DeepSeek-V3 shape this allows up to 28 tokens per call, DeepSeek-V2-Lite 92, eva's own
+ *     H5120 / 384-expert shape 48). Every call takes the decode kernel, whatever its row count.
+ *   - Argument errors (EVA_ERR_INVALID) and the size check (EVA_ERR_WORKSPACE) are reported before
+ *     any device call.
  *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress)
  *     with that device current; make that first call before any stream capture.
  *   - All calls share the one array, which keeps the previous call's contents. Each call clears
@@ -181,7 +184,9 @@ int eva_moe_experts_noalloc(const EvaMoeShape* shape, const void* x, int32_t x_i
                             const int64_t* const* tables, const int64_t* shared,
                             float* out_f32, void* out_bf16, int32_t* status_out, void* stream);
 
-/* ---- expert parallelism (one process per GPU; the exchange itself is NCCL all-to-all) ----------
+/* ---- expert parallelism (one process per GPU; rows move by this library's peer-memory stores over
+ * NVLink (eva_ep_dispatch_peers / eva_ep_combine_peers) or, with the plan and pack below, by NCCL
+ * send/recv and all-to-all issued by the host) ----------------------------------------------------
  * No counterpart in the reference, which has no expert parallelism: these replace the kernel-side
  * local-expert filter slot_info (runtime/ds41/csrc/moe_coop2048/vendor/exl3_moe_coop_kernel.cuh:208-223)
  * and the empty-row path write_empty_row_chunk (:573-610) with an explicit dispatch and combine.

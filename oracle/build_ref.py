@@ -6,7 +6,7 @@ copied). The headers use torch's c10 headers for TORCH_CHECK and cuBLAS headers,
 directories are added; nothing from torch is linked. Output goes only to oracle/_ref/ (git-ignored,
 travels to the GPU box with the tree).
 
-Usage: python oracle/build_ref.py [/path/to/reference]
+Usage: python oracle/build_ref.py [/path/to/reference]   (default: $EVA_REFERENCE, else ../reference)
 """
 from __future__ import annotations
 
@@ -19,8 +19,21 @@ HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "libref_coop.so"
 
 
+def reference_root() -> Path | None:
+    """The reference checkout: $EVA_REFERENCE, else a folder named `reference` beside this repository."""
+    env = os.environ.get("EVA_REFERENCE")
+    if env:
+        return Path(env)
+    sibling = HERE.parent.parent / "reference"
+    return sibling if sibling.is_dir() else None
+
+
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVA_REFERENCE", "/root/reference"))
+    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else reference_root()
+    if ref is None:
+        print("no reference checkout (argument, EVA_REFERENCE, or a 'reference' folder beside this repository); "
+              "oracle/_ref not built")
+        return 1
     src = ref / "runtime" / "ds41" / "csrc" / "moe_coop2048"
     if not (src / "vendor" / "quant" / "exl3_moe_coop_kernel.cuh").exists():
         print(f"reference sources not found under {src}; oracle/_ref not built")

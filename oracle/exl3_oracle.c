@@ -181,6 +181,14 @@ void eo_tile_pos(int p, int* k, int* n)
     *k = 2 * (l & 3) + (j & 1) + 8 * ((j >> 1) & 1);
 }
 
+/* eo_mul1_decode of every 16-bit state, filled once (the dequantization reads it per weight). */
+static uint16_t eo_mul1_table[65536];
+
+__attribute__((constructor)) static void eo_mul1_ctor(void)
+{
+    for (uint32_t s = 0; s < 65536; ++s) eo_mul1_table[s] = eo_mul1_decode(s);
+}
+
 /* Dequantize a whole projection. trellis: int16 [in/16][out/16][16K]; w: fp16 bits [in][out]. */
 void eo_dequant(const int16_t* trellis, int in, int out, int K, uint16_t* w)
 {
@@ -192,7 +200,7 @@ void eo_dequant(const int16_t* trellis, int in, int out, int K, uint16_t* w)
         for (int nt = 0; nt < nt_n; ++nt) {
             const uint32_t* tile = (const uint32_t*) (trellis) + ((size_t) kt * nt_n + nt) * words;
             for (int p = 0; p < 256; ++p) {
-                uint16_t h = eo_mul1_decode(eo_tile_state2(tile, K, p));
+                uint16_t h = eo_mul1_table[eo_tile_state2(tile, K, p)];
                 w[(size_t) (kt * 16 + kk[p]) * out + nt * 16 + nn[p]] = h;
             }
         }
@@ -233,12 +241,17 @@ void eo_linear(const double* x, int M, int in, int out, const uint16_t* suh, con
         eo_had128_blocks(xr, in);
         if (round_in)
             for (int i = 0; i < in; ++i) xr[i] = F16(eo_f64_to_f16(xr[i]));
-        for (int j = 0; j < out; ++j) acc[j] = 0.0;
-        for (int i = 0; i < in; ++i) {
-            const double xi = xr[i];
-            if (xi == 0.0) continue;
-            const uint16_t* wr = w + (size_t) i * out;
-            for (int j = 0; j < out; ++j) acc[j] += xi * F16(wr[j]);
+        /* each output column sums its products in input order; columns are split over threads */
+        #pragma omp parallel for schedule(static)
+        for (int j0 = 0; j0 < out; j0 += 256) {
+            const int j1 = j0 + 256 < out ? j0 + 256 : out;
+            for (int j = j0; j < j1; ++j) acc[j] = 0.0;
+            for (int i = 0; i < in; ++i) {
+                const double xi = xr[i];
+                if (xi == 0.0) continue;
+                const uint16_t* wr = w + (size_t) i * out;
+                for (int j = j0; j < j1; ++j) acc[j] += xi * F16(wr[j]);
+            }
         }
         eo_had128_blocks(acc, out);
         for (int j = 0; j < out; ++j) y[(size_t) m * out + j] = acc[j] * F16(svh[j]);

@@ -32,7 +32,10 @@ OUT = Path(__file__).resolve().parent
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVA_REFERENCE", "/root/reference"))
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVA_REFERENCE")
+    if not ref:
+        sys.exit("pass the reference checkout's root as the first argument or set EVA_REFERENCE")
+    ref = Path(ref)
     sys.path.insert(0, str(ref / "runtime"))
     import torch
     import ds41.cpu_precision_reference as cpr

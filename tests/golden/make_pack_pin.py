@@ -75,7 +75,10 @@ def write_checkpoint(d: Path, cfg, layers) -> None:
 
 
 def main():
-    ref = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVA_REFERENCE", "/root/reference"))
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("EVA_REFERENCE")
+    if not ref:
+        sys.exit("pass the reference checkout's root as the first argument or set EVA_REFERENCE")
+    ref = Path(ref)
     cfg, layers = pin_layers()
     with tempfile.TemporaryDirectory() as tmp:
         ckpt, out = Path(tmp) / "ckpt", Path(tmp) / "pack"

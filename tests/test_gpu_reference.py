@@ -130,7 +130,8 @@ def test_moe_matches_reference_kernels(ref, oracle, cfg, M):
 def test_speed_vs_reference_kernels(ref, capsys):
     """Routed experts of the DeepSeek-V3 decode step (batch 8, K3, 4.24 GB of experts): the reference's
     prepare/rot/A/B launches vs eva_moe_experts, same routes, CUDA events, a different batch every
-    iteration (working set larger than L2). Prints both times; asserts only that both ran."""
+    iteration (working set larger than L2). Prints both times and checks that the two outputs of the
+    last batch agree (max-rel-err <= 2e-2, cosine >= 0.9999)."""
     cfg = C.V3.with_(shared_inter=0)
     layer_d = make_layer(cfg, DEV, seed=0)
     M, iters = 8, 20
@@ -141,7 +142,7 @@ def test_speed_vs_reference_kernels(ref, capsys):
     xs = [torch.randn(M, cfg.hidden, device=DEV).half() for _ in range(iters + 3)]
     from eva_b200.runner import EvaMoERunner
     r = EvaMoERunner(DEV, topk=cfg.topk, hidden=cfg.hidden, inter=cfg.inter, max_rows=M, n_experts=cfg.n_experts)
-    times = {}
+    times, outs = {}, {}
     for name in ("reference", "eva"):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         for i in range(iters + 3):
@@ -149,16 +150,22 @@ def test_speed_vs_reference_kernels(ref, capsys):
                 torch.cuda.synchronize()
                 ev[0].record()
             if name == "reference":
-                ref_coop(ref, layer_d, xs[i], sels[i], rw16, cfg.bits, 0.0)
+                y = ref_coop(ref, layer_d, xs[i], sels[i], rw16, cfg.bits, 0.0)
             else:
-                r.run(xs[i], sels[i], rw16, tuple(layer_d.packed.unbind(0)), cfg.bits, 0.0, check_bounds=False)
+                y = r.run(xs[i], sels[i], rw16, tuple(layer_d.packed.unbind(0)), cfg.bits, 0.0, check_bounds=False)
         ev[1].record()
         torch.cuda.synchronize()
         times[name] = ev[0].elapsed_time(ev[1]) / iters
+        outs[name] = y.double().cpu().numpy().ravel()
+    a, b = outs["eva"], outs["reference"]
+    err = np.abs(a - b).max() / np.abs(b).max()
+    cos = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
     with capsys.disabled():
         print(f"\nV3 decode routed experts, batch {M}, K3: reference {times['reference']:.3f} ms/step, "
-              f"eva {times['eva']:.3f} ms/step, speed-up {times['reference'] / times['eva']:.2f}x")
+              f"eva {times['eva']:.3f} ms/step, speed-up {times['reference'] / times['eva']:.2f}x; "
+              f"eva vs reference max-rel-err {err:.2e}, cosine {cos:.7f}")
     assert times["reference"] > 0 and times["eva"] > 0
+    assert err <= 2e-2 and cos >= 0.9999
 
 
 def test_prefill_speed_vs_reference_kernels(ref, capsys):
