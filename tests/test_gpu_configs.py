@@ -114,9 +114,10 @@ def _skewed_routes(cfg, M, hot, rng):
     """Routes in which expert hot[i][0] is chosen by the first hot[i][1] rows, the remaining slots
     of every row filled with distinct random experts."""
     sel = np.zeros((M, cfg.topk), dtype=np.int64)
+    hot_ids = {e for e, _ in hot}
     for m in range(M):
         chosen = [e for e, n in hot if m < n]
-        rest = [e for e in rng.permutation(cfg.n_experts) if e not in chosen][: cfg.topk - len(chosen)]
+        rest = [e for e in rng.permutation(cfg.n_experts) if e not in hot_ids][: cfg.topk - len(chosen)]
         row = np.array(chosen + rest)
         sel[m] = row[rng.permutation(cfg.topk)]
     rw = (rng.random((M, cfg.topk)) + 0.1).astype(np.float32)
