@@ -65,6 +65,9 @@ def parse():
     ap.add_argument("--stack-layers", type=int, default=58)
     ap.add_argument("--residency", type=float, default=1.0,
                     help="--stack: fraction of each rank's experts resident on the device (misses from pinned host)")
+    ap.add_argument("--decode-microbench", action="store_true",
+                    help="the EXL3 decode loop alone (tiles resident in shared memory): decoded weights per SM clock "
+                         "of each decode design, against the rate HBM streaming needs")
     ap.add_argument("--ep-transport", default="peers", choices=["peers", "nccl"],
                     help="N > 1: rows exchanged through NVLink peer memory by this library's kernels, or NCCL")
     return ap.parse_args()
@@ -654,6 +657,74 @@ def stack_bench(args, cfg, dev, rank, world, local):
         dist.destroy_process_group()
 
 
+MICRO_VARIANTS = {
+    0: "mma.sync decode of the fused decode kernel (4 words + 2 funnel shifts per lane-tile, mul1 byte sums, "
+       "fp16 pairs, mma.m16n8k16)",
+    1: "two-word decode -> mul1 products -> tcgen05.st into TMEM (kind::i8 operand form), no MMA",
+    2: "two-word decode -> raw codebook fp16 -> tcgen05.st into TMEM (kind::f16 operand form), no MMA",
+    3: "variant 1 + tcgen05.mma.kind::i8 with A in TMEM (M 128, N 16), 7-slot TMEM ring, one issuing thread",
+    4: "variant 2 + tcgen05.mma.kind::f16 with A in TMEM, same ring",
+    5: "variant 1 without the ALU/FMA split of the window extraction",
+    6: "two-word decode (2 words + 2 funnel shifts per lane-tile) + mma.m16n8k16, pairs packed by IMAD",
+    7: "variant 6 with pairs packed by PRMT",
+    8: "variant 7 with 2 windows extracted as multiply + shift (FMA pipe)",
+    9: "variant 6 with 2 windows extracted as multiply + shift",
+    10: "variant 7 with 4 windows extracted as multiply + shift",
+    11: "variant 8 with a stage's bookkeeping around each pass (B fragments from shared memory, mbarrier arrive + "
+        "wait, warp barrier)",
+    12: "the fused kernel's pipeline: a producer warp streams 32 trellis rows + 8 B rows per stage from a 1 GB buffer "
+        "(HBM) into a 4-stage ring, 16 decoding warps as variant 8",
+    13: "variant 12 with a 32 MB source (resident in L2)",
+    14: "variant 12 with 5 ring stages",
+    15: "variant 12 with decoders not waiting for the data (shared-memory contention only)",
+    16: "variant 12 with one contiguous copy per stage instead of 32 row copies",
+    17: "variant 12 with one 2-D tensor copy (TMA tensor map over the strided rows) per stage",
+    18: "variant 12 with the stage copied by cp.async 16-byte copies from the producer warp",
+}
+
+
+def decode_microbench(args):
+    """One JSON line: decoded weights per SM clock of each decode design (eva_decode_microbench)."""
+    import ctypes
+    import torch
+    from eva_b200 import _lib
+    lib = _lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    hbm, hbm_kind = peaks()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    clocks = ClockSampler(0).__enter__()
+    clocks.wait_first()
+    c0 = clocks.mark()
+    res = {}
+    for bits in (3, 2, 4):
+        for v in sorted(MICRO_VARIANTS):
+            out = (ctypes.c_double * 5)()
+            _lib.check(lib.eva_decode_microbench(v, bits, 64, out, stream), "eva_decode_microbench")   # warm-up
+            # about 50 ms per measurement
+            iters = max(64, int(64 * 50.0 / max(out[4], 1e-3)))
+            _lib.check(lib.eva_decode_microbench(v, bits, iters, out, stream), "eva_decode_microbench")
+            res[f"K{bits}_v{v}"] = {"weights_per_sm_clock": out[0], "sm_clocks": out[1], "ms": out[4],
+                                    "weights": out[2], "device_status": int(out[3])}
+    time.sleep(0.06)
+    c1 = clocks.mark()
+    clocks.__exit__(None, None, None)
+    cs = clocks.summary(c0, c1)
+    f_ghz = (cs["sm_mhz"] or 1965.0) / 1000.0
+    need = {b: hbm * 1e9 / (b / 8.0) / sms / (f_ghz * 1e9) for b in (2, 3, 4)}
+    line = {"metric": "decode_loop_weights_per_sm_clock", "unit": "weights / SM / clock",
+            "value": res["K3_v0"]["weights_per_sm_clock"],
+            "config": {"workload": "EXL3 decode loop alone, trellis tiles resident in shared memory (no HBM), one "
+                                   "CTA per SM, clock64 per CTA", "variants": MICRO_VARIANTS},
+            "results": res,
+            "hbm_rate_needs_weights_per_sm_clock": {f"K{b}": need[b] for b in need},
+            "hbm_peak": {"gbs": hbm, "kind": hbm_kind, "sm_clock_ghz": f_ghz},
+            "ceiling_frac_of_hbm": {k: r["weights_per_sm_clock"] / need[int(k[1])] for k, r in res.items()},
+            "clocks": cs}
+    print(json.dumps(line), flush=True)
+
+
 def dataclasses_replace(obj, **kw):
     import dataclasses
     return dataclasses.replace(obj, **kw)
@@ -663,6 +734,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
+    if args.decode_microbench:
+        return decode_microbench(args)
     import numpy as np
     import torch
     import torch.distributed as dist

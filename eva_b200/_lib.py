@@ -22,7 +22,8 @@ EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_stat
            "eva_moe_arch", "eva_moe_experts_noalloc", "eva_moe_experts_decode", "eva_moe_experts_prefill",
            "eva_ep_dispatch", "eva_ep_combine", "eva_ep_arena_layout", "eva_peer_alloc", "eva_peer_open",
            "eva_peer_close", "eva_peer_free", "eva_ep_dispatch_peers", "eva_ep_wait_rows", "eva_ep_signal_partials",
-           "eva_ep_combine_peers", "eva_rmsnorm_residual", "eva_moe_experts_window")
+           "eva_ep_combine_peers", "eva_rmsnorm_residual", "eva_moe_experts_window", "eva_decode_microbench",
+           "eva_tc_selftest")
 EP_MAX_WORLD = 32
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -113,6 +114,10 @@ def load(build_if_missing: bool = True):
                                          vp, vp, vp]
     L.eva_rmsnorm_residual.restype = ctypes.c_int
     L.eva_rmsnorm_residual.argtypes = [i32, i32, vp, vp, vp, i32, ctypes.c_float, vp, vp]
+    L.eva_decode_microbench.restype = ctypes.c_int
+    L.eva_decode_microbench.argtypes = [i32, i32, i32, P(ctypes.c_double), vp]
+    L.eva_tc_selftest.restype = ctypes.c_int
+    L.eva_tc_selftest.argtypes = [i32, vp, vp, vp, vp, vp]
     L.eva_moe_arch.restype = i32
     L.eva_moe_arch.argtypes = []
     _lib = L

@@ -14,8 +14,9 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libeva_moe.so"
-SOURCES = ["capi.cu", "routing.cu", "router_tc.cu", "experts.cu", "prefill.cu", "noalloc.cu", "ep.cu", "stack.cu"]
-HEADERS = ["common.cuh", "internal.h", "tc.cuh"]
+SOURCES = ["capi.cu", "routing.cu", "router_tc.cu", "experts.cu", "prefill.cu", "noalloc.cu", "ep.cu", "stack.cu",
+           "decode_bench.cu"]
+HEADERS = ["common.cuh", "internal.h", "tc.cuh", "decode_tc.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -91,6 +91,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     }
 }
 
+// mbar_wait for warps that are not on the critical path (they sleep ns nanoseconds between tries, so a
+// long wait does not take issue slots from the warps doing the work). Same bound and status rules.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, int* status, uint32_t ns)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    if (ld_volatile(status) & ST_TIMEOUT) return false;
+    for (;;) {
+        __nanosleep(ns);
+        if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer() - t0 > WAIT_LIMIT_NS || (ld_volatile(status) & ST_TIMEOUT)) {
+            atomicOr(status, ST_TIMEOUT);
+            return false;
+        }
+    }
+}
+
 // Global -> shared bulk copy completing on an mbarrier. dst, src 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
 {

@@ -9,17 +9,24 @@
 //
 // Work items are claimed from a global counter in phase order (all rotations, then all gate/up
 // chunks, then all down chunks). An item only ever waits (bounded) on items with smaller indices,
-// which were claimed earlier by running CTAs, so the schedule cannot deadlock.
+// which were claimed earlier by running CTAs, so the schedule cannot deadlock; an epilogue never
+// waits on anything but its own CTA's partial sums.
 //
-// Per CTA: 1 producer warp streams the item's trellis rows with 1-D bulk copies (TMA, one
-// CTA per copy) into a 4-stage shared-memory ring (32 k-tile rows x 128 columns per stage); 16
-// consumer warps each decode 4 rows x 4 tiles per stage in registers and run mma.m16n8k16 with
-// the weights as the 16 x 16 A operand (rows = output columns) and up to 8 tokens as the B
-// operand, accumulating in fp32. The MMA takes the raw codebook values h = 1024 + bytesum and the
-// affine map of the codebook is applied to the sums (see decode_raw). Each warp follows the item
-// sequence on its own; the only CTA-wide barriers are the cross-warp k reduction at the end of a
-// projection, the rotation items and the split-k hand-off. The epilogue of a run row is done by
-// one warp while the others go on to the next item.
+// Per CTA (warp specialised):
+//   warp 16      producer: claims items and streams their trellis rows with 1-D bulk copies (TMA,
+//                one CTA per copy) into a 4-stage shared-memory ring (32 k-tile rows x 128 columns
+//                per stage), writing each item's geometry, run and slots into the stage header
+//   warps 0..15  decoders: each decodes 4 rows x 4 tiles per stage in registers (two words and two
+//                funnel shifts per lane and tile, window extraction split between the ALU and FMA
+//                pipes) and runs mma.m16n8k16 with the weights as the 16 x 16 A operand (rows =
+//                output columns) and up to 8 tokens as B, accumulating in fp32. The MMA takes the
+//                raw codebook values h = 1024 + bytesum and the codebook's affine map is applied to
+//                the sums (see decode_raw). At a projection's end they store their partial sums
+//                and go straight on; rotation items are done by these 16 warps together.
+//   warps 17..20 epilogue: sum the 8 k-quads of a projection's partials (mbarrier hand-off, the
+//                partial buffer is released right after), then the item's epilogue (split-k
+//                publication, Hadamard / scales / activation or the combine) while the decoders
+//                already run the next item.
 //
 // Reference behaviour (paths within Findddx/eva, runtime/ds41/csrc/moe_coop2048/vendor/quant/):
 //   exl3_moe_coop_kernel.cuh:634-671 (rotation), :680-809 (gate/up GEMV + epilogue),
@@ -27,19 +34,25 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "decode_tc.cuh"
 #include "internal.h"
 
 namespace eva {
 
-constexpr int NCW = 16;                    // consumer warps
-constexpr int THREADS = (NCW + 1) * 32;    // + producer warp
+constexpr int NCW = 16;                    // decoding warps (warps 0..15)
+constexpr int NEW = 4;                     // epilogue warps (warps 17..20; warp 16 is the trellis producer)
+constexpr int BPW = NCW + 1 + NEW;         // the B producer warp (21)
+constexpr int THREADS = (NCW + 2 + NEW) * 32;
 constexpr int NSTAGE = 4;
-constexpr int STAGE_KT = 32;               // k-tile rows per stage (4 per consumer warp pair)
+constexpr int STAGE_KT = 32;               // k-tile rows per stage (4 per decoding warp pair)
 constexpr int NT = 8;                      // 16-column tiles per item (128 output columns)
-constexpr int STAGE_BYTES = STAGE_KT * NT * 32 * 4;   // sized for K = 4
-constexpr int RED_FLOATS = NCW * 4 * 4 * 32;  // [warp][tile][c][lane]
+constexpr int STAGE_BYTES = STAGE_KT * NT * 32 * 4;   // trellis of a stage, sized for K = 4
+constexpr int BROW_BYTES = STAGE_KT * 32;              // one token row of B for the stage's k-tile rows (fp16)
+constexpr int STAGE_TOTAL = STAGE_BYTES + RUN_ROWS * BROW_BYTES;   // + the run's 8 B rows
 constexpr int RES_FLOATS = 2 * RUN_ROWS * 128;
-constexpr size_t SMEM_BYTES = static_cast<size_t>(NSTAGE) * STAGE_BYTES + RED_FLOATS * 4 + RES_FLOATS * 4 + 1024;
+constexpr int PART_F4 = NCW * 4 * 32;      // one projection's partial sums: [warp][tile][lane] float4
+constexpr size_t SMEM_BYTES =
+    static_cast<size_t>(NSTAGE) * STAGE_TOTAL + PART_F4 * 16 + RES_FLOATS * 4 + (4 * NSTAGE + 2) * 8;
 
 struct KParams {
     // shape
@@ -206,62 +219,69 @@ __device__ __forceinline__ void store4_frag(__half* row, int k0, const float (&v
 }
 
 // ---------------------------------------------------------------------------------------------
-// Consumers. A stage holds 32 k-tile rows x 8 tiles (128 output columns). Warp w takes k-tile rows
-// 4 (w / 2) .. 4 (w / 2) + 3 of the stage and tiles 4 (w % 2) .. 4 (w % 2) + 3, i.e. 16 tiles and
-// 16 fp32 accumulator registers; the eight warps of one column half split k and are summed at the
-// end of a projection.
+// Decoding warps. A stage holds 32 k-tile rows x 8 tiles (128 output columns). Warp w takes k-tile
+// rows 4 (w / 2) .. 4 (w / 2) + 3 of the stage and tiles 4 (w % 2) .. 4 (w % 2) + 3, i.e. 16 tiles
+// and 16 fp32 accumulator registers; the eight warps of one column half split k. At the end of a
+// projection each warp stores its partial sums to shared memory and goes on with the next stage;
+// the epilogue warps sum the eight k-quads and run the item's epilogue meanwhile.
 
 constexpr int WT = 4;   // tiles per warp per k-tile row
 constexpr int WR = 4;   // k-tile rows per warp per stage
 
-// B fragments of the 4 k-tile rows 4 g .. 4 g + 3 for lane `lane`: one 32-byte contiguous read
-// (row = fragment-layout input row of the lane's token).
-__device__ __forceinline__ void load_b4(const __half* row, int g, int lane, uint32_t (&b)[2 * WR])
+// B fragments of the 4 k-tile rows 4 g .. 4 g + 3 of a stage for lane `lane`: one 32-byte contiguous
+// shared-memory read from the stage's copy of the lane's token row (fragment layout).
+__device__ __forceinline__ void load_b4_smem(const uint8_t* brow, int g, int lane, uint32_t (&b)[2 * WR])
 {
-    const uint4* p = reinterpret_cast<const uint4*>(row + g * 64 + (lane & 3) * 16);
-    const uint4 u0 = __ldcg(p), u1 = __ldcg(p + 1);
+    const uint4* p = reinterpret_cast<const uint4*>(brow + g * 128 + (lane & 3) * 32);
+    const uint4 u0 = p[0], u1 = p[1];
     b[0] = u0.x; b[1] = u0.y; b[2] = u0.z; b[3] = u0.w;
     b[4] = u1.x; b[5] = u1.y; b[6] = u1.z; b[7] = u1.w;
 }
 
+
+// One GEMV stage of a decoding warp: k-tile rows 4 quad .. 4 quad + 3 of the stage (those below ke)
+// x tiles 4 whalf .. 4 whalf + 3, B fragments of those rows in b. The two words of every tile of the
+// next row are loaded while the current row is decoded, so the shared-memory latency of a row's
+// words overlaps the previous row's arithmetic.
 template <int K>
-__device__ __forceinline__ void gemv_row(const uint32_t* tiles, const LaneGrp& d, uint32_t b0, uint32_t b1,
-                                         float (&acc)[WT][4])
+__device__ __forceinline__ void gemv_stage(const uint32_t* buf, const LaneW& d, int quad, int whalf, int r0, int ke,
+                                           const uint32_t (&b)[2 * WR], float (&acc)[WT][4])
 {
+    const uint32_t* rowp = buf + ((WR * quad) * NT + WT * whalf) * 8 * K;
+    const int nr = min(WR, ke - r0);
+    uint32_t w[2][WT][2];
 #pragma unroll
     for (int t = 0; t < WT; ++t) {
-        uint32_t a[4];
-        decode_raw<K>(tiles + t * 8 * K, d, a);
-        mma_16816(acc[t], a, b0, b1);
+        w[0][t][0] = rowp[t * 8 * K + d.w0];
+        w[0][t][1] = rowp[t * 8 * K + d.w1];
+    }
+#pragma unroll
+    for (int r = 0; r < WR; ++r) {
+        if (r >= nr) break;
+        const int cb = r & 1, nb = cb ^ 1;
+        if (r + 1 < WR && r + 1 < nr) {
+#pragma unroll
+            for (int t = 0; t < WT; ++t) {
+                w[nb][t][0] = rowp[(r + 1) * NT * 8 * K + t * 8 * K + d.w0];
+                w[nb][t][1] = rowp[(r + 1) * NT * 8 * K + t * 8 * K + d.w1];
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < WT; ++t) {
+            uint32_t s[8], h[8], a[4];
+            lane_states_w<K, 2>(w[cb][t][0], w[cb][t][1], d, s);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) h[j] = mul1_sum(s[j]);
+            a[0] = __byte_perm(h[0], h[1], 0x5410);
+            a[1] = __byte_perm(h[4], h[5], 0x5410);
+            a[2] = __byte_perm(h[2], h[3], 0x5410);
+            a[3] = __byte_perm(h[6], h[7], 0x5410);
+            mma_16816(acc[t], a, b[2 * r], b[2 * r + 1]);
+        }
     }
 }
 
-// Sum of the 8 k-split accumulators of each column half into res[tok][col] (natural layout).
-__device__ __forceinline__ void reduce_acc(float (&acc)[WT][4], float* red, float* res, int tid, int warp, int lane)
-{
-#pragma unroll
-    for (int t = 0; t < WT; ++t)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) red[((warp * WT + t) * 4 + c) * 32 + lane] = acc[t][c];
-    named_sync(1, NCW * 32);
-    for (int v = tid; v < 2 * WT * 4 * 32; v += NCW * 32) {
-        const int half = v >> 9, r = v & 511;        // r = (t * 4 + c) * 32 + lane
-        float sum = 0.0f;
-#pragma unroll
-        for (int pr = 0; pr < NCW / 2; ++pr) sum += red[(2 * pr + half) * WT * 4 * 32 + r];
-        const int l = r & 31, c = (r >> 5) & 3, t = r >> 7;
-        const int col = (half * WT + t) * 16 + (l >> 2) + 8 * (c >> 1);
-        const int tok = 2 * (l & 3) + (c & 1);
-        res[tok * 128 + col] = CB_C0 * sum;
-    }
-    named_sync(1, NCW * 32);
-#pragma unroll
-    for (int t = 0; t < WT; ++t)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) acc[t][c] = 0.0f;
-}
-
-// Item state of one consumer warp (each warp follows the item sequence on its own).
+// Item state of one warp (each warp follows the item sequence on its own).
 struct WarpItem {
     Geo g;
     RunInfo ri;
@@ -269,31 +289,160 @@ struct WarpItem {
 };
 
 // Ring stage header written by the producer: the item and its stage, and at the item's first stage
-// its geometry, run and the run's slots (the producer has them already; the 16 consumer warps copy
-// them instead of each repeating the chain of dependent global loads).
+// its geometry, run and the run's slots (the producer has them already; the decoding warps read
+// them from here instead of each repeating the chain of dependent global loads).
 struct StageHdr {
     int item, s;
     WarpItem wi;
 };
 
-// Epilogue operands prefetched at item start by the warp that runs the epilogue of row `warp`:
-// type 1: svh_gate, svh_up, suh_down of the chunk; type 2: svh_down (fp16 x 4 per lane).
-struct EpiOps {
-    uint2 v[3][32];
+// What the decoding warps hand to the epilogue warps with each projection's partial sums.
+struct PartInfo {
+    int item, proj, last;   // item -1: no more work; last: the item's final projection
+    WarpItem wi;
 };
+
+// Gate/up epilogue of row t (one warp): g, u = H128(res) * svh (+ the codebook's affine term when
+// with_corr), a = act(g, u), a' = fp16(H128(a * suh_down)) stored in fragment layout with its
+// per-chunk sum, then the run's gate/up completion counter.
+__device__ __forceinline__ void epi_gateup_row(const KParams& p, const WarpItem& wi, const float* res, int t,
+                                               bool with_corr, int lane)
+{
+    const Geo& g = wi.g;
+    const RunInfo& ri = wi.ri;
+    const size_t S_tot = static_cast<size_t>(p.S_cap) + p.M;
+    const int nchH = p.H / 128;
+    const int sl = wi.slot[t];
+    const int col = g.chunk * 128 + lane * 4;
+    float gv[4], uv[4], sv[4];
+    float t0 = 0.0f, t1 = 0.0f;
+    if (with_corr) {
+        const float* xs0 = p.xsum + static_cast<size_t>(sl) * nchH;
+        const float* xs1 = p.xsum + (S_tot + sl) * nchH;
+        for (int c = g.kb / 8 + lane; c < g.ke / 8; c += 32) {
+            t0 += __ldcg(xs0 + c);
+            t1 += __ldcg(xs1 + c);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+            t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        gv[i] = res[t * 128 + lane * 4 + i] + CB_C1 * t0;
+        uv[i] = res[RUN_ROWS * 128 + t * 128 + lane * 4 + i] + CB_C1 * t1;
+    }
+    had128_warp(gv, lane);
+    had128_warp(uv, lane);
+    load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 2)) + col, sv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) gv[i] *= sv[i];
+    load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 5)) + col, sv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) uv[i] *= sv[i];
+    const int mode = ri.shared ? p.act_shared : p.act_routed;
+    float av[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) av[i] = act_gated(gv[i], uv[i], p.limit, mode);
+    load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 7)) + col, sv);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) av[i] *= sv[i];
+    had128_warp(av, lane);
+    store4_frag(p.act + static_cast<size_t>(sl) * p.ipad, col, av);
+    float sm = 0.0f;   // sum of the values as stored (fp16)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) sm += __half2float(__float2half_rn(av[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    if (lane == 0) p.asum[static_cast<size_t>(sl) * (p.imax / 128) + g.chunk] = sm;
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) atomicAdd(&p.ctrA[g.run], 1);
+}
+
+// Down epilogue of row t (one warp): v = H128(res + affine term) * svh_down * routing weight into the
+// slot's partial row; the last arrival of (token, chunk) sums the token's slots in slot order, then
+// the shared expert, and stores the output row.
+__device__ __forceinline__ void epi_down_row(const KParams& p, const WarpItem& wi, const float* res, int t, int lane)
+{
+    const Geo& g = wi.g;
+    const RunInfo& ri = wi.ri;
+    const int sl = wi.slot[t];
+    const int tok = slot_token(p, sl);
+    const int col = g.chunk * 128 + lane * 4;
+    const float* as = p.asum + static_cast<size_t>(sl) * (p.imax / 128);
+    float t0 = 0.0f;
+    for (int c = lane; c < ri.I / 128; c += 32) t0 += __ldcg(as + c);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+    float v[4], sv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = res[t * 128 + lane * 4 + i] + CB_C1 * t0;
+    had128_warp(v, lane);
+    load4_half_ro(static_cast<const __half*>(tensor_ptr(p, ri, 8)) + col, sv);
+    const float wgt = ri.shared ? 1.0f : p.rw[sl];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = v[i] * sv[i] * wgt;
+    *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(sl) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
+    __threadfence();
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+        const int old = atomicAdd(&p.ctrB[tok * (p.H / 128) + g.chunk], 1);
+        last = old == p.tok_expect[tok] - 1;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (!last) return;
+    __threadfence();
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < p.topk; ++k) {
+        const int s2 = tok * p.topk + k;
+        if (!p.slot_act[s2]) continue;
+        const float4 d = __ldcg(reinterpret_cast<const float4*>(p.dpart + static_cast<size_t>(s2) * p.H + col));
+        o[0] += d.x;
+        o[1] += d.y;
+        o[2] += d.z;
+        o[3] += d.w;
+    }
+    if (p.has_shared && tok >= p.sh0 && tok < p.sh0 + p.shn) {
+        const float4 d =
+            __ldcg(reinterpret_cast<const float4*>(p.dpart + (static_cast<size_t>(p.S_cap) + tok) * p.H + col));
+        o[0] += d.x;
+        o[1] += d.y;
+        o[2] += d.z;
+        o[3] += d.w;
+    }
+    const size_t oi = static_cast<size_t>(tok) * p.H + col;
+    if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + oi) = make_float4(o[0], o[1], o[2], o[3]);
+    if (p.out_bf16) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(o[2], o[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&lo);
+        u.y = *reinterpret_cast<uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(p.out_bf16 + oi) = u;
+    }
+}
 
 template <int KR, int KS>
 __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint32_t* ring = reinterpret_cast<uint32_t*>(smem);
-    float* red = reinterpret_cast<float*>(smem + static_cast<size_t>(NSTAGE) * STAGE_BYTES);
-    float* res = red + RED_FLOATS;   // [2][8][128]
-    uint64_t* full = reinterpret_cast<uint64_t*>(res + RES_FLOATS);
-    uint64_t* empty = full + NSTAGE;
+    float4* part = reinterpret_cast<float4*>(smem + static_cast<size_t>(NSTAGE) * STAGE_TOTAL);   // [warp][t][lane]
+    float* res = reinterpret_cast<float*>(part + PART_F4);                                         // [2][8][128]
+    uint64_t* full = reinterpret_cast<uint64_t*>(res + RES_FLOATS);   // trellis of the stage landed
+    uint64_t* empty = full + NSTAGE;       // the decoders are done with the stage
+    uint64_t* hready = empty + NSTAGE;     // the stage header is written (trellis producer -> B producer)
+    uint64_t* bfull = hready + NSTAGE;     // the stage's B rows landed (or there are none)
+    uint64_t* pfull = bfull + NSTAGE;      // decoders -> epilogue warps: one projection's partial sums written
+    uint64_t* pfree = pfull + 1;           // epilogue warps -> decoders: partial sums consumed
     __shared__ StageHdr hdr[NSTAGE];
-    __shared__ WarpItem wis[NCW];
-    __shared__ EpiOps eps[RUN_ROWS];
+    __shared__ PartInfo pinfo;
+    __shared__ PartInfo epi;               // the epilogue warps' copy of the item they finish
+    __shared__ WarpItem wi0;               // decoder warp 0's copy of its current item
     __shared__ int sh_flag;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -301,7 +450,11 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
         for (int i = 0; i < NSTAGE; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], NCW);
+            mbar_init(&hready[i], 1);
+            mbar_init(&bfull[i], 1);
         }
+        mbar_init(pfull, NCW);
+        mbar_init(pfree, NEW);
         fence_barrier_init();
     }
     __syncthreads();
@@ -328,7 +481,7 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
             for (int s = 0; s < g.nstages; ++s, ++q) {
                 const int slot = q % NSTAGE;
                 const uint32_t ph = (q / NSTAGE) & 1;
-                mbar_wait(&empty[slot], ph ^ 1, p.status);
+                mbar_wait_sleep(&empty[slot], ph ^ 1, p.status, 100);
                 int nvalid = 0;
                 const uint8_t* src = nullptr;
                 size_t row_stride = 0;
@@ -354,39 +507,182 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                 if (item >= 0 && s == 0 && lane < RUN_ROWS)
                     hdr[slot].wi.slot[lane] = lane < ri.nrows ? run_slot(p, g.run, lane) : run_slot(p, g.run, 0);
                 __syncwarp();
-                if (lane == 0) mbar_arrive_expect_tx(&full[slot], nvalid * row_bytes);
+                if (lane == 0) {
+                    mbar_arrive(&hready[slot]);
+                    mbar_arrive_expect_tx(&full[slot], nvalid * row_bytes);
+                }
                 __syncwarp();
-                if (lane < nvalid)
-                    bulk_g2s(ring + slot * (STAGE_BYTES / 4) + lane * (row_bytes / 4), src + lane * row_stride, row_bytes,
-                             &full[slot]);
+                uint32_t* st = ring + slot * (STAGE_TOTAL / 4);
+                if (lane < nvalid) bulk_g2s(st + lane * (row_bytes / 4), src + lane * row_stride, row_bytes, &full[slot]);
             }
             if (item < 0) break;
         }
         return;
     }
 
-    // ---------------------------------------------------------------------- consumers
+    if (warp == BPW) {
+        // ------------------------------------------------------------------ B producer
+        // Follows the stage headers. At an item's start it waits (bounded) for the item's inputs,
+        // which other items write (rotation, gate/up epilogues), so that the trellis producer never
+        // blocks on them; then per stage it copies the run's 8 token rows of B for the stage's k-tile
+        // rows into the stage (lane t: row t; rows past the run repeat row 0).
+        int cur_item = -2, type = -1, bslot = 0, kb = 0, ke = 0, nsp = 1;
+        for (uint32_t q = 0;; ++q) {
+            const int slot = q % NSTAGE;
+            const uint32_t ph = (q / NSTAGE) & 1;
+            mbar_wait_sleep(&hready[slot], ph, p.status, 32);
+            const int item = hdr[slot].item;
+            const int s = hdr[slot].s;
+            if (item < 0) break;
+            if (item != cur_item) {
+                cur_item = item;
+                const WarpItem& hw = hdr[slot].wi;
+                type = hw.g.type;
+                kb = hw.g.kb;
+                ke = hw.g.ke;
+                nsp = hw.g.nsp;
+                bslot = hw.slot[lane < RUN_ROWS ? lane : 0];
+                if (type != 0 && lane == 0) {
+                    if (type == 1) wait_geq(&p.ctr0[hw.g.run], 1, p.status);
+                    else wait_geq(&p.ctrA[hw.g.run], (hw.ri.I / 128) * hw.ri.nrows, p.status);
+                    // written by generic-proxy stores of other CTAs, read below by bulk copies (async proxy)
+                    asm volatile("fence.proxy.async.global;" ::: "memory");
+                }
+                __syncwarp();
+            }
+            if (type != 1 && type != 2) {
+                if (lane == 0) mbar_arrive(&bfull[slot]);
+                continue;
+            }
+            const int proj = type == 2 ? 0 : s / nsp;
+            const int kt0 = kb + (s % nsp) * STAGE_KT;
+            const int nvalid = min(STAGE_KT, ke - kt0);
+            const __half* brow = type == 1 ? p.xrot + (static_cast<size_t>(proj) * (p.S_cap + p.M) + bslot) * p.hpad
+                                           : p.act + static_cast<size_t>(bslot) * p.ipad;
+            if (lane == 0) mbar_arrive_expect_tx(&bfull[slot], nvalid * RUN_ROWS * 32);
+            __syncwarp();
+            if (lane < RUN_ROWS)
+                bulk_g2s(ring + slot * (STAGE_TOTAL / 4) + (STAGE_BYTES + lane * BROW_BYTES) / 4,
+                         brow + static_cast<size_t>(kt0) * 16, nvalid * 32, &bfull[slot]);
+        }
+        return;
+    }
+
+    if (warp > NCW) {
+        // ------------------------------------------------------------------ epilogue warps
+        // Per projection end: sum the 8 k-quads' partials into res, release the partial buffer, and
+        // after an item's last projection run its epilogue (split-k publication, row epilogues).
+        const int ew = warp - NCW - 1, etid = tid - (NCW + 1) * 32;
+        for (uint32_t pe = 0;; ++pe) {
+            if (!mbar_wait_sleep(pfull, pe & 1, p.status, 500)) break;
+            static_assert(sizeof(PartInfo) % 4 == 0 && sizeof(PartInfo) / 4 <= NEW * 32, "PartInfo copy");
+            if (etid < static_cast<int>(sizeof(PartInfo) / 4))
+                reinterpret_cast<int*>(&epi)[etid] = reinterpret_cast<const int*>(&pinfo)[etid];
+            named_sync(2, NEW * 32);
+            if (epi.item < 0) break;
+            float* rs = res + epi.proj * RUN_ROWS * 128;
+            for (int cmb = etid; cmb < 2 * WT * 32; cmb += NEW * 32) {
+                const int wh = cmb >> 7, t = (cmb >> 5) & 3, l = cmb & 31;
+                float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int qd = 0; qd < NCW / 2; ++qd) {
+                    const float4 v = part[((2 * qd + wh) * WT + t) * 32 + l];
+                    a.x += v.x;
+                    a.y += v.y;
+                    a.z += v.z;
+                    a.w += v.w;
+                }
+                // D fragment of mma.m16n8k16: c0 (col g, tok 2t') c1 (g, 2t'+1) c2 (g+8, 2t') c3 (g+8, 2t'+1)
+                const int col = (wh * WT + t) * 16 + (l >> 2), tok = 2 * (l & 3);
+                rs[tok * 128 + col] = CB_C0 * a.x;
+                rs[(tok + 1) * 128 + col] = CB_C0 * a.y;
+                rs[tok * 128 + col + 8] = CB_C0 * a.z;
+                rs[(tok + 1) * 128 + col + 8] = CB_C0 * a.w;
+            }
+            named_sync(2, NEW * 32);
+            if (lane == 0) mbar_arrive(pfree);
+            if (!epi.last) continue;
+            const WarpItem& wi = epi.wi;
+            const Geo& g = wi.g;
+            const int nrows = wi.ri.nrows;
+            if (g.type == 1) {
+                bool with_corr = true;
+                if (p.split_a > 1) {
+                    // this split's sums (with the affine term of its k range) to global; the last split
+                    // of (run, chunk) sums them and runs the row epilogues
+                    const size_t S_tot = static_cast<size_t>(p.S_cap) + p.M;
+                    const int nchH = p.H / 128;
+                    for (int t = ew; t < nrows; t += NEW) {
+                        const int sl = wi.slot[t];
+                        float t0 = 0.0f, t1 = 0.0f;
+                        for (int c = g.kb / 8 + lane; c < g.ke / 8; c += 32) {
+                            t0 += __ldcg(p.xsum + static_cast<size_t>(sl) * nchH + c);
+                            t1 += __ldcg(p.xsum + (S_tot + sl) * nchH + c);
+                        }
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+                            t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+                        }
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            res[t * 128 + lane * 4 + i] += CB_C1 * t0;
+                            res[RUN_ROWS * 128 + t * 128 + lane * 4 + i] += CB_C1 * t1;
+                        }
+                    }
+                    named_sync(2, NEW * 32);
+                    const int pidx = (g.run * (p.imax / 128) + g.chunk) * p.split_a + g.ks;
+                    float* dst = p.partA + static_cast<size_t>(pidx) * RES_FLOATS;
+                    for (int i = etid; i < RES_FLOATS; i += NEW * 32) dst[i] = res[i];
+                    __threadfence();
+                    named_sync(2, NEW * 32);
+                    if (etid == 0) {
+                        const int old = atomicAdd(&p.ctrAk[g.run * (p.imax / 128) + g.chunk], 1);
+                        sh_flag = old == p.split_a - 1;
+                    }
+                    named_sync(2, NEW * 32);
+                    const int last = sh_flag;
+                    named_sync(2, NEW * 32);
+                    if (!last) continue;
+                    __threadfence();
+                    const float* base =
+                        p.partA + static_cast<size_t>((g.run * (p.imax / 128) + g.chunk) * p.split_a) * RES_FLOATS;
+                    for (int i = etid; i < RES_FLOATS; i += NEW * 32) {
+                        float a = 0.0f;
+                        for (int k = 0; k < p.split_a; ++k) a += __ldcg(base + static_cast<size_t>(k) * RES_FLOATS + i);
+                        res[i] = a;
+                    }
+                    named_sync(2, NEW * 32);
+                    with_corr = false;
+                }
+                for (int t = ew; t < nrows; t += NEW) epi_gateup_row(p, wi, res, t, with_corr, lane);
+            } else {
+                for (int t = ew; t < nrows; t += NEW) epi_down_row(p, wi, res, t, lane);
+            }
+            named_sync(2, NEW * 32);   // res is read by the row epilogues until here
+        }
+        return;
+    }
+
+    // ---------------------------------------------------------------------- decoders
     float acc[WT][4];
 #pragma unroll
     for (int t = 0; t < WT; ++t)
 #pragma unroll
         for (int c = 0; c < 4; ++c) acc[t][c] = 0.0f;
 
-    const LaneGrp dR = lane_grp<KR>(lane);
-    const LaneGrp dS = lane_grp<KS>(lane);
+    const LaneW dR = lane_w<KR>(lane);
+    const LaneW dS = lane_w<KS>(lane);
     const int quad = warp >> 1, whalf = warp & 1;
     const size_t S_tot = static_cast<size_t>(p.S_cap) + p.M;
     const int nchH = p.H / 128;
-    WarpItem& wi = wis[warp];
-    uint32_t q = 0;
-    uint32_t bc[2 * WR], bn[2 * WR];   // B of this warp's WR rows: current stage / next stage
-#pragma unroll
-    for (int i = 0; i < 2 * WR; ++i) bc[i] = bn[i] = 0;
-    float tsp[2] = {0.0f, 0.0f};       // epilogue warps: per-lane partial input sums (gate/up or down)
+    uint32_t q = 0, pq = 0;
+    uint32_t bc[2 * WR];               // B fragments of this warp's WR rows of the stage
     int cur_item = -2;
+    // the current item, in registers
+    int type = -1, run = 0, nsp = 1, kb = 0, ke = 0, nstages = 1;
+    bool shared_run = false;
     int sp = 0, proj = 0;              // stage within the projection, projection (0 gate / 1 up)
-    const __half* brow = nullptr;      // this lane's token row of the B input (projection 0)
-    size_t bproj = 0;                  // element offset from the gate to the up input
     for (;; ++q) {
         const int slot = q % NSTAGE;
         const uint32_t ph = (q / NSTAGE) & 1;
@@ -394,68 +690,37 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
         const int item = hdr[slot].item;
         const int s = hdr[slot].s;
         if (item < 0) break;
+        mbar_wait(&bfull[slot], ph, p.status);
+        const WarpItem& hw = hdr[slot].wi;
         if (item != cur_item) {
-            // item start, per warp: geometry, the run's slots, the dependency, epilogue prefetch
+            // item start: geometry into registers, the B row, the dependency
             cur_item = item;
-            if (lane == 0) {
-                wi.g = hdr[slot].wi.g;
-                wi.ri = hdr[slot].wi.ri;
-            }
-            if (lane < RUN_ROWS) wi.slot[lane] = hdr[slot].wi.slot[lane];
-            __syncwarp();
-            const Geo g = wi.g;
-            const RunInfo ri = wi.ri;
+            type = hw.g.type;
+            run = hw.g.run;
+            nsp = hw.g.nsp;
+            kb = hw.g.kb;
+            ke = hw.g.ke;
+            nstages = hw.g.nstages;
+            shared_run = hw.ri.shared;
             sp = 0;
             proj = 0;
-            __syncwarp();
-            {
-                const int bs = wi.slot[lane >> 2];   // this lane's token row (rows past the run repeat row 0)
-                if (g.type == 1) {
-                    brow = p.xrot + static_cast<size_t>(bs) * p.hpad;
-                    bproj = S_tot * p.hpad;
-                } else {
-                    brow = p.act + static_cast<size_t>(bs) * p.ipad;
-                    bproj = 0;
+            if (warp == 0) {
+                if (lane < RUN_ROWS) wi0.slot[lane] = hw.slot[lane];
+                if (lane == 0) {
+                    wi0.g = hw.g;
+                    wi0.ri = hw.ri;
                 }
-            }
-            if (lane == 0) {
-                if (g.type == 1) wait_geq(&p.ctr0[g.run], 1, p.status);
-                if (g.type == 2) wait_geq(&p.ctrA[g.run], (ri.I / 128) * ri.nrows, p.status);
-            }
-            __syncwarp();
-            if (g.type != 0 && warp < ri.nrows) {
-                const int sl = wi.slot[warp];
-                const int col = g.chunk * 128 + lane * 4;
-                if (g.type == 1) {
-                    cp_async8(&eps[warp].v[0][lane], static_cast<const __half*>(tensor_ptr(p, ri, 2)) + col);
-                    cp_async8(&eps[warp].v[1][lane], static_cast<const __half*>(tensor_ptr(p, ri, 5)) + col);
-                    cp_async8(&eps[warp].v[2][lane], static_cast<const __half*>(tensor_ptr(p, ri, 7)) + col);
-                    const float* xs0 = p.xsum + static_cast<size_t>(sl) * nchH;
-                    const float* xs1 = p.xsum + (S_tot + sl) * nchH;
-                    tsp[0] = tsp[1] = 0.0f;
-                    for (int c = g.kb / 8 + lane; c < g.ke / 8; c += 32) {
-                        tsp[0] += __ldcg(xs0 + c);
-                        tsp[1] += __ldcg(xs1 + c);
-                    }
-                } else {
-                    cp_async8(&eps[warp].v[0][lane], static_cast<const __half*>(tensor_ptr(p, ri, 8)) + col);
-                    const float* as = p.asum + static_cast<size_t>(sl) * (p.imax / 128);
-                    tsp[0] = 0.0f;
-                    for (int c = lane; c < ri.I / 128; c += 32) tsp[0] += __ldcg(as + c);
-                }
-                cp_async_commit();
             }
         }
-        const int type = wi.g.type;
 
         if (type == 0) {
-            // rotation of the run's rows for gate (suh row 1) and up (suh row 4); CTA-wide
-            const RunInfo ri = wi.ri;
+            // rotation of the run's rows for gate (suh row 1) and up (suh row 4); decoders only
+            const RunInfo ri = hw.ri;
             const int nch = p.H / 128;
             const int units = ri.nrows * 2 * nch;
             for (int u = warp; u < units; u += NCW) {
                 const int t = u / (2 * nch), rem = u % (2 * nch), pj = rem / nch, c = rem % nch;
-                const int sl = wi.slot[t];
+                const int sl = hw.slot[t];
                 const int tok = slot_token(p, sl);
                 const int col = c * 128 + lane * 4;
                 float v[4], su[4];
@@ -473,39 +738,24 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                 if (lane == 0) p.xsum[(static_cast<size_t>(pj) * S_tot + sl) * nchH + c] = sm;
             }
             __threadfence();
+            __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
             named_sync(1, NCW * 32);
-            if (tid == 0) atomicAdd(&p.ctr0[wi.g.run], 1);
+            if (tid == 0) atomicAdd(&p.ctr0[run], 1);
             continue;
         }
 
-        // GEMV stage: rows 4 quad .. 4 quad + 3 of the stage, B fragments prefetched one stage ahead
-        const int nsp = wi.g.nsp, kb = wi.g.kb, ke = wi.g.ke, nstages = wi.g.nstages;
-        const bool shared_run = wi.ri.shared;
+        // GEMV stage: rows 4 quad .. 4 quad + 3 of the stage; B from the stage's copy of the run's rows
         const int kt0 = kb + sp * STAGE_KT;
         const int r0 = kt0 + WR * quad;
-        if (s == 0) {
-            load_b4(brow, (kt0 >> 2) + quad, lane, bc);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 2 * WR; ++i) bc[i] = bn[i];
-        }
+        const uint8_t* stage_base = reinterpret_cast<const uint8_t*>(ring + slot * (STAGE_TOTAL / 4));
+        load_b4_smem(stage_base + STAGE_BYTES + (lane >> 2) * BROW_BYTES, quad, lane, bc);
         const int sp1 = sp + 1 == nsp ? 0 : sp + 1;
         const int proj1 = sp + 1 == nsp ? proj + 1 : proj;
-        if (s + 1 < nstages) load_b4(brow + proj1 * bproj, ((kb + sp1 * STAGE_KT) >> 2) + quad, lane, bn);
         {
-            const uint32_t* buf = ring + slot * (STAGE_BYTES / 4);
-            if (!shared_run || KR == KS) {
-                const uint32_t* rowp = buf + ((WR * quad) * NT + WT * whalf) * 8 * KR;
-#pragma unroll
-                for (int r = 0; r < WR; ++r)
-                    if (r0 + r < ke) gemv_row<KR>(rowp + r * NT * 8 * KR, dR, bc[2 * r], bc[2 * r + 1], acc);
-            } else {
-                const uint32_t* rowp = buf + ((WR * quad) * NT + WT * whalf) * 8 * KS;
-#pragma unroll
-                for (int r = 0; r < WR; ++r)
-                    if (r0 + r < ke) gemv_row<KS>(rowp + r * NT * 8 * KS, dS, bc[2 * r], bc[2 * r + 1], acc);
-            }
+            const uint32_t* buf = reinterpret_cast<const uint32_t*>(stage_base);
+            if (!shared_run || KR == KS) gemv_stage<KR>(buf, dR, quad, whalf, r0, ke, bc, acc);
+            else gemv_stage<KS>(buf, dS, quad, whalf, r0, ke, bc, acc);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
@@ -515,163 +765,32 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
         sp = sp1;
         proj = proj1;
         if (!proj_end) continue;
-        reduce_acc(acc, red, res + cproj * RUN_ROWS * 128, tid, warp, lane);
-        if (s != nstages - 1) continue;
-
-        // ------------------------------------------------------------- item epilogues
-        const Geo g = wi.g;
-        const RunInfo ri = wi.ri;
-        if (type == 1) {
-            if (p.split_a > 1) {
-                // publish this split's partial sums (input-sum correction included); the last
-                // split of (run, chunk) finishes. CTA-wide.
-                if (warp < ri.nrows) {
-                    float t0 = tsp[0], t1 = tsp[1];
+        // hand this projection's partial sums to the epilogue warps
+        mbar_wait(pfree, (pq & 1) ^ 1, p.status);
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        t0 += __shfl_xor_sync(0xffffffffu, t0, o);
-                        t1 += __shfl_xor_sync(0xffffffffu, t1, o);
-                    }
+        for (int t = 0; t < WT; ++t) {
+            part[(warp * WT + t) * 32 + lane] = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        res[warp * 128 + lane * 4 + i] += CB_C1 * t0;
-                        res[RUN_ROWS * 128 + warp * 128 + lane * 4 + i] += CB_C1 * t1;
-                    }
-                    tsp[0] = tsp[1] = 0.0f;
-                }
-                named_sync(1, NCW * 32);
-                const int pidx = (g.run * (p.imax / 128) + g.chunk) * p.split_a + g.ks;
-                float* dst = p.partA + static_cast<size_t>(pidx) * RES_FLOATS;
-                for (int i = tid; i < RES_FLOATS; i += NCW * 32) dst[i] = res[i];
-                __threadfence();
-                named_sync(1, NCW * 32);
-                if (tid == 0) {
-                    const int old = atomicAdd(&p.ctrAk[g.run * (p.imax / 128) + g.chunk], 1);
-                    sh_flag = old == p.split_a - 1;
-                }
-                named_sync(1, NCW * 32);
-                const int last = sh_flag;
-                named_sync(1, NCW * 32);
-                if (!last) {
-                    if (warp < ri.nrows) cp_async_wait_all();
-                    continue;
-                }
-                __threadfence();
-                const float* base = p.partA + static_cast<size_t>((g.run * (p.imax / 128) + g.chunk) * p.split_a) * RES_FLOATS;
-                for (int i = tid; i < RES_FLOATS; i += NCW * 32) {
-                    float a = 0.0f;
-                    for (int k = 0; k < p.split_a; ++k) a += __ldcg(base + static_cast<size_t>(k) * RES_FLOATS + i);
-                    res[i] = a;
-                }
-                named_sync(1, NCW * 32);
-            }
-            if (warp < ri.nrows) {
-                // this warp's row: output rotation, scales, activation, down-input rotation
-                const int t = warp, sl = wi.slot[t];
-                const int col = g.chunk * 128 + lane * 4;
-                float t0 = tsp[0], t1 = tsp[1];
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    t0 += __shfl_xor_sync(0xffffffffu, t0, o);
-                    t1 += __shfl_xor_sync(0xffffffffu, t1, o);
-                }
-                float gv[4], uv[4], sv[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    gv[i] = res[t * 128 + lane * 4 + i] + CB_C1 * t0;
-                    uv[i] = res[RUN_ROWS * 128 + t * 128 + lane * 4 + i] + CB_C1 * t1;
-                }
-                cp_async_wait_all();
-                __syncwarp();
-                had128_warp(gv, lane);
-                had128_warp(uv, lane);
-                load4_half(reinterpret_cast<const __half*>(&eps[t].v[0][lane]), sv);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) gv[i] *= sv[i];
-                load4_half(reinterpret_cast<const __half*>(&eps[t].v[1][lane]), sv);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) uv[i] *= sv[i];
-                const int mode = ri.shared ? p.act_shared : p.act_routed;
-                float av[4];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) av[i] = act_gated(gv[i], uv[i], p.limit, mode);
-                load4_half(reinterpret_cast<const __half*>(&eps[t].v[2][lane]), sv);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) av[i] *= sv[i];
-                had128_warp(av, lane);
-                store4_frag(p.act + static_cast<size_t>(sl) * p.ipad, col, av);
-                float sm = 0.0f;   // sum of the values as stored (fp16)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) sm += __half2float(__float2half_rn(av[i]));
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
-                if (lane == 0) p.asum[static_cast<size_t>(sl) * (p.imax / 128) + g.chunk] = sm;
-                __threadfence();
-                __syncwarp();
-                if (lane == 0) atomicAdd(&p.ctrA[g.run], 1);
-            }
-        } else if (warp < ri.nrows) {
-            // down epilogue of this warp's row: rotate, scale, weight; the last arrival of
-            // (token, chunk) combines the token's slots in slot order, then the shared expert
-            const int t = warp, sl = wi.slot[t];
-            const int tok = slot_token(p, sl);
-            const int col = g.chunk * 128 + lane * 4;
-            float t0 = tsp[0];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) t0 += __shfl_xor_sync(0xffffffffu, t0, o);
-            float v[4], sv[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] = res[t * 128 + lane * 4 + i] + CB_C1 * t0;
-            cp_async_wait_all();
-            __syncwarp();
-            had128_warp(v, lane);
-            load4_half(reinterpret_cast<const __half*>(&eps[t].v[0][lane]), sv);
-            const float wgt = ri.shared ? 1.0f : p.rw[sl];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] = v[i] * sv[i] * wgt;
-            *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(sl) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
-            __threadfence();
-            __syncwarp();
-            int last = 0;
+            for (int c = 0; c < 4; ++c) acc[t][c] = 0.0f;
+        }
+        if (warp == 0) {
+            if (lane < static_cast<int>(sizeof(WarpItem) / 4))
+                reinterpret_cast<int*>(&pinfo.wi)[lane] = reinterpret_cast<const int*>(&wi0)[lane];
             if (lane == 0) {
-                const int old = atomicAdd(&p.ctrB[tok * (p.H / 128) + g.chunk], 1);
-                last = old == p.tok_expect[tok] - 1;
-            }
-            last = __shfl_sync(0xffffffffu, last, 0);
-            if (last) {
-                __threadfence();
-                float o[4] = {0.f, 0.f, 0.f, 0.f};
-                for (int k = 0; k < p.topk; ++k) {
-                    const int s2 = tok * p.topk + k;
-                    if (!p.slot_act[s2]) continue;
-                    const float4 d = __ldcg(reinterpret_cast<const float4*>(p.dpart + static_cast<size_t>(s2) * p.H + col));
-                    o[0] += d.x;
-                    o[1] += d.y;
-                    o[2] += d.z;
-                    o[3] += d.w;
-                }
-                if (p.has_shared && tok >= p.sh0 && tok < p.sh0 + p.shn) {
-                    const float4 d = __ldcg(reinterpret_cast<const float4*>(
-                        p.dpart + (static_cast<size_t>(p.S_cap) + tok) * p.H + col));
-                    o[0] += d.x;
-                    o[1] += d.y;
-                    o[2] += d.z;
-                    o[3] += d.w;
-                }
-                const size_t oi = static_cast<size_t>(tok) * p.H + col;
-                if (p.out_f32) *reinterpret_cast<float4*>(p.out_f32 + oi) = make_float4(o[0], o[1], o[2], o[3]);
-                if (p.out_bf16) {
-                    __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]);
-                    __nv_bfloat162 hi = __floats2bfloat162_rn(o[2], o[3]);
-                    uint2 u;
-                    u.x = *reinterpret_cast<uint32_t*>(&lo);
-                    u.y = *reinterpret_cast<uint32_t*>(&hi);
-                    *reinterpret_cast<uint2*>(p.out_bf16 + oi) = u;
-                }
+                pinfo.item = cur_item;
+                pinfo.proj = cproj;
+                pinfo.last = s == nstages - 1;
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(pfull);
+        ++pq;
     }
-    cp_async_wait_all();
+    // no more items: tell the epilogue warps
+    mbar_wait(pfree, (pq & 1) ^ 1, p.status);
+    if (warp == 0 && lane == 0) pinfo.item = -1;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(pfull);
 }
 
 using ExpertsKernel = void (*)(KParams);

@@ -285,6 +285,30 @@ int eva_rmsnorm_residual(int32_t H, int32_t M, float* resid, const float* add, c
 /* Library identification: sm arch the kernels were built for (100 for sm_100a). */
 int32_t eva_moe_arch(void);
 
+/* ---- measurement and self-test entry points (no counterpart in the reference) ----------------
+ *
+ * eva_decode_microbench: the EXL3 decode loop alone, on trellis tiles resident in shared memory (no
+ * HBM traffic), one CTA per SM. variant 0: the mma.sync decode of the fused decode kernel; 1 / 2:
+ * decode into tensor memory (mul1 products for kind::i8 / raw codebook fp16 for kind::f16), no MMA;
+ * 3 / 4: the same with tcgen05.mma reading A from tensor memory through a slot ring; 5: variant 1
+ * without splitting the window extraction between the ALU and FMA pipes; 6..10: the two-word decode
+ * with mma.sync (pair packing by IMAD or PRMT, 0 / 2 / 4 windows extracted on the FMA pipe); 11:
+ * variant 8 with a fused-kernel stage's bookkeeping around each pass; 12 / 13: variant 8 fed by
+ * the fused kernel's bulk-copy ring from a 1 GB (HBM) / 32 MB (L2) source, allocated by the call;
+ * 14: 5 ring stages; 15: decoders not waiting for the data; 16: one contiguous copy per stage;
+ * 17: one 2-D tensor copy per stage; 18: cp.async 16-byte copies by the producer warp.
+ * bits: EXL3 K (2..4).
+ * out[5] = {decoded weights per SM clock, SM clocks of the launch (max over CTAs), weights decoded,
+ * device status bits, event time of the launch in ms}. Synchronises the stream.
+ *
+ * eva_tc_selftest: one CTA checks a tensor-memory layout. what 0: out[128][16] u32 = TMEM read back
+ * (32x32b) after 16x256b.x2 stores of tags (half << 12 | lane << 4 | register) at lanes 32 w + 16 half;
+ * what 1: out[128][16] s32 = A x B^T with A u8 [128][32] stored in TMEM, B s8 [16][32] in shared
+ * memory (tcgen05.mma.kind::i8); what 2: out[128][16] f32 = A x B^T with A f16 [128][16] in TMEM and
+ * B f16 [16][16] (kind::f16). a, b: device arrays of those shapes (what > 0); status: device int32. */
+int eva_decode_microbench(int32_t variant, int32_t bits, int32_t iters, double* out, void* stream);
+int eva_tc_selftest(int32_t what, const uint32_t* a, const uint32_t* b, uint32_t* out, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
