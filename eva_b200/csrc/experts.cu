@@ -33,9 +33,12 @@
 //   :816-963 (down GEMV + combine + shared merge); exl3_dq.cuh / codebook.cuh (decode).
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "decode_tc.cuh"
 #include "internal.h"
+#include "tc.cuh"
 
 namespace eva {
 
@@ -86,6 +89,7 @@ struct KParams {
     // outputs
     float* out_f32;
     __nv_bfloat16* out_bf16;
+    CUtensorMap* tmaps;       // [grid][DEC_MAP_SETS][2] per-item tensor maps (workspace)
 };
 
 struct RunInfo {
@@ -426,8 +430,15 @@ __device__ __forceinline__ void epi_down_row(const KParams& p, const WarpItem& w
     }
 }
 
+// Template tensor maps of the trellis of one projection, viewed as [in/16 k-tile rows][out/16 x 32K
+// bytes] in 8-byte elements with a box of 8 tiles (one 128-column chunk) x STAGE_KT rows: routed
+// gate/up, routed down, shared gate/up, shared down. Their global address is replaced per item.
+struct TrellisMaps {
+    CUtensorMap gu, dn, sgu, sdn;
+};
+
 template <int KR, int KS>
-__global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
+__global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, const __grid_constant__ TrellisMaps tm)
 {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint32_t* ring = reinterpret_cast<uint32_t*>(smem);
@@ -444,6 +455,7 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
     __shared__ PartInfo epi;               // the epilogue warps' copy of the item they finish
     __shared__ WarpItem wi0;               // decoder warp 0's copy of its current item
     __shared__ int sh_flag;
+    __shared__ __align__(128) CUtensorMap tm_edit[2];   // the producer's staging copies of an item's maps
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
@@ -463,8 +475,13 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
 
     if (warp == NCW) {
         // ------------------------------------------------------------------ producer
-        uint32_t q = 0;
-        for (;;) {
+        // One 2-D tensor copy per stage (32 strided trellis rows of the item's 128-column chunk): many
+        // small bulk copies per stage throttle the copy engine. Per item the projection's tensor
+        // map(s) are written into this CTA's slot set (item_seq % DEC_MAP_SETS); a set is rewritten
+        // only after NSTAGE + 1 later items, by which time every copy that read it has landed (each
+        // item has at least one stage and a stage slot is refilled only after its decoders released it).
+        uint32_t q = 0, item_seq = 0;
+        for (;; ++item_seq) {
             int item = 0;
             if (lane == 0) item = atomicAdd(p.ctr_work, 1);
             item = __shfl_sync(0xffffffffu, item, 0);
@@ -478,23 +495,33 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                 g.nstages = 1;
                 g.type = -1;
             }
+            const CUtensorMap* maps = nullptr;
+            if (g.type == 1 || g.type == 2) {
+                CUtensorMap* gm = p.tmaps + (static_cast<size_t>(blockIdx.x) * DEC_MAP_SETS + item_seq % DEC_MAP_SETS) * 2;
+                const CUtensorMap* tmpl = g.type == 1 ? (ri.shared ? &tm.sgu : &tm.gu) : (ri.shared ? &tm.sdn : &tm.dn);
+                const int nmap = g.type == 1 ? 2 : 1;
+                for (int j = 0; j < nmap; ++j)
+                    reinterpret_cast<uint32_t*>(&tm_edit[j])[lane] = reinterpret_cast<const uint32_t*>(tmpl)[lane];
+                __syncwarp();
+                if (lane == 0)
+                    for (int j = 0; j < nmap; ++j) tmap_replace_addr(&tm_edit[j], tensor_ptr(p, ri, (g.type == 1 ? j : 2) * 3));
+                __syncwarp();
+                for (int j = 0; j < nmap; ++j) tmap_copy_release(gm + j, &tm_edit[j]);
+                if (lane == 0)
+                    for (int j = 0; j < nmap; ++j) tmap_acquire(gm + j);
+                __syncwarp();
+                maps = gm;
+            }
             for (int s = 0; s < g.nstages; ++s, ++q) {
                 const int slot = q % NSTAGE;
                 const uint32_t ph = (q / NSTAGE) & 1;
                 mbar_wait_sleep(&empty[slot], ph ^ 1, p.status, 100);
-                int nvalid = 0;
-                const uint8_t* src = nullptr;
-                size_t row_stride = 0;
-                uint32_t row_bytes = 0;
+                int kt0 = 0, proj = 0;
+                uint32_t stage_bytes = 0;
                 if (g.type == 1 || g.type == 2) {
-                    const int proj = g.type == 2 ? 2 : s / g.nsp;      // 0 gate, 1 up, 2 down
-                    const int kt0 = g.kb + (s % g.nsp) * STAGE_KT;
-                    nvalid = min(STAGE_KT, g.ke - kt0);
-                    const int out = g.type == 2 ? p.H : ri.I;
-                    row_bytes = NT * 32 * ri.K;                          // 8 tiles of 32K bytes
-                    row_stride = static_cast<size_t>(out / 16) * 32 * ri.K;
-                    src = static_cast<const uint8_t*>(tensor_ptr(p, ri, proj * 3)) + static_cast<size_t>(kt0) * row_stride +
-                          static_cast<size_t>(g.chunk) * row_bytes;
+                    proj = g.type == 2 ? 0 : s / g.nsp;                  // map index: 0 gate / down, 1 up
+                    kt0 = g.kb + (s % g.nsp) * STAGE_KT;
+                    stage_bytes = STAGE_KT * NT * 32 * ri.K;             // the full box (rows past the tensor read 0)
                 }
                 if (lane == 0) {
                     hdr[slot].item = item;
@@ -509,11 +536,11 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
                 __syncwarp();
                 if (lane == 0) {
                     mbar_arrive(&hready[slot]);
-                    mbar_arrive_expect_tx(&full[slot], nvalid * row_bytes);
+                    mbar_arrive_expect_tx(&full[slot], stage_bytes);
+                    if (stage_bytes)
+                        tma_load_2d(ring + slot * (STAGE_TOTAL / 4), maps + proj, g.chunk * NT * 4 * ri.K, kt0, &full[slot]);
                 }
                 __syncwarp();
-                uint32_t* st = ring + slot * (STAGE_TOTAL / 4);
-                if (lane < nvalid) bulk_g2s(st + lane * (row_bytes / 4), src + lane * row_stride, row_bytes, &full[slot]);
             }
             if (item < 0) break;
         }
@@ -793,7 +820,22 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p)
     if (lane == 0) mbar_arrive(pfull);
 }
 
-using ExpertsKernel = void (*)(KParams);
+using ExpertsKernel = void (*)(KParams, TrellisMaps);
+
+// Template map of a projection's trellis [in/16][out/16][16K] int16 as [in/16][out/16 x 4K] 8-byte
+// elements, box 8 tiles x STAGE_KT rows; base: any 16-byte aligned device address (replaced per item).
+static bool encode_trellis_map(CUtensorMap* m, void* base, int in, int out, int K)
+{
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(out / 16) * 4 * K, static_cast<cuuint64_t>(in / 16)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(out / 16) * 32 * K};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(NT * 4 * K), STAGE_KT};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
 
 static ExpertsKernel pick_kernel(int kr, int ks)
 {
@@ -855,6 +897,7 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
     p.status = reinterpret_cast<int*>(ws + L.status);
     p.out_f32 = a.out_f32;
     p.out_bf16 = static_cast<__nv_bfloat16*>(a.out_bf16);
+    p.tmaps = reinterpret_cast<CUtensorMap*>(ws + L.tmaps);
 
     // split the gate/up k range when there are too few gate/up items to fill the GPU
     const int sms = num_sms();
@@ -867,11 +910,16 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
         split *= 2;
     p.split_a = split;
 
+    TrellisMaps tm;
+    const int ish = p.I_sh ? p.I_sh : p.I;
+    if (!encode_trellis_map(&tm.gu, ws, p.H, p.I, p.K) || !encode_trellis_map(&tm.dn, ws, p.I, p.H, p.K) ||
+        !encode_trellis_map(&tm.sgu, ws, p.H, ish, p.K_sh) || !encode_trellis_map(&tm.sdn, ws, ish, p.H, p.K_sh))
+        return cudaErrorInvalidValue;
     const ExpertsKernel kern = pick_kernel(p.K, p.K_sh);
     if (!kern) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES));
     if (e != cudaSuccess) return e;
-    kern<<<sms, THREADS, SMEM_BYTES, stream>>>(p);
+    kern<<<std::min(sms, DEC_MAX_CTAS), THREADS, SMEM_BYTES, stream>>>(p, tm);
     return cudaGetLastError();
 }
 

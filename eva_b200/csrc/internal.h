@@ -21,6 +21,7 @@ struct WsLayout {
     size_t logits, wsplit, idx, w, xrot, act, dpart, partA, xsum, asum, total;
     size_t tstart, pxg, pxu, pap;   // prefill: tile prefix, sorted rotated inputs, sorted down inputs
     size_t pscan;                   // multi-CTA permutation: per-chunk expert counts and prefixes
+    size_t tmaps;                   // decode kernel: per-CTA tensor maps of the items in flight
     int max_split;   // largest gate/up k-split the partial buffer allows (1 = none)
     int hpad, ipad;  // row widths (halves) of the fragment-layout input buffers (one stage of slack)
 };
@@ -98,6 +99,8 @@ struct ExpertsArgs {
 cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream);
 cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream);
 
+constexpr int DEC_MAX_CTAS = 256;       // decode kernel grid cap (tensor-map slots per CTA in the workspace)
+constexpr int DEC_MAP_SETS = 5;         // tensor-map sets per CTA: one per item, reused after NSTAGE + 1 items
 constexpr int PREFILL_MIN_ROWS = 129;   // eva_moe_experts takes the tensor-core path from this many rows
 constexpr int PF_TILE_ROWS = 256;       // rows of one expert per tensor-core CTA (two 128-row MMA halves)
 

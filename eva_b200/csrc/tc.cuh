@@ -99,6 +99,32 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
 }
 
+// Tensor maps edited on the device (per-item global addresses). A template map is copied into
+// shared memory, its global address replaced, and the result copied to a global slot with a release
+// fence for the tensor-map proxy; the thread that issues tensor copies with it acquires first.
+__device__ __forceinline__ void tmap_replace_addr(void* smem_map, const void* gaddr)
+{
+    asm volatile("tensormap.replace.tile.global_address.shared::cta.b1024.b64 [%0], %1;" ::"r"(smem_u32(smem_map)),
+                 "l"(reinterpret_cast<uint64_t>(gaddr))
+                 : "memory");
+}
+
+// Whole warp (aligned): 128-byte copy shared -> global with a release fence for the tensor-map proxy.
+__device__ __forceinline__ void tmap_copy_release(void* gmap, const void* smem_map)
+{
+    asm volatile(
+        "tensormap.cp_fenceproxy.global.shared::cta.tensormap::generic.release.gpu.sync.aligned [%0], [%1], 128;" ::"l"(
+            reinterpret_cast<uint64_t>(gmap)),
+        "r"(smem_u32(smem_map))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmap_acquire(const void* gmap)
+{
+    asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(reinterpret_cast<uint64_t>(gmap))
+                 : "memory");
+}
+
 // Round a dynamic shared-memory pointer up to the 1024-byte alignment of 128B-swizzled tiles.
 __device__ __forceinline__ uint8_t* align1024(uint8_t* raw)
 {
