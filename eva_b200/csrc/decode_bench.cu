@@ -150,7 +150,6 @@ __global__ void __launch_bounds__((MB_DEC + 1) * 32, 1) mb_stream(int iters, con
                                                                  const uint8_t* bsrc, unsigned long long* cyc,
                                                                  int* status, const __grid_constant__ CUtensorMap tmap)
 {
-    constexpr bool CONTIG = MODE == 1;
     constexpr int MS_NSTAGE = NST;
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ uint64_t full[MS_NSTAGE], empty[MS_NSTAGE];

@@ -55,7 +55,7 @@ constexpr int STAGE_TOTAL = STAGE_BYTES + RUN_ROWS * BROW_BYTES;   // + the run'
 constexpr int RES_FLOATS = 2 * RUN_ROWS * 128;
 constexpr int PART_F4 = NCW * 4 * 32;      // one projection's partial sums: [warp][tile][lane] float4
 constexpr size_t SMEM_BYTES =
-    static_cast<size_t>(NSTAGE) * STAGE_TOTAL + PART_F4 * 16 + RES_FLOATS * 4 + (4 * NSTAGE + 2) * 8;
+    static_cast<size_t>(NSTAGE) * STAGE_TOTAL + PART_F4 * 16 + RES_FLOATS * 4 + (3 * NSTAGE + 2) * 8;
 
 struct KParams {
     // shape
@@ -243,45 +243,32 @@ __device__ __forceinline__ void load_b4_smem(const uint8_t* brow, int g, int lan
 }
 
 
+template <int K>
+__device__ __forceinline__ void gemv_row_w(const uint32_t* tiles, const LaneW& d, uint32_t b0, uint32_t b1,
+                                           float (&acc)[WT][4])
+{
+#pragma unroll
+    for (int t = 0; t < WT; ++t) {
+        uint32_t a[4];
+        decode_afrag_w<K, 2, true>(tiles + t * 8 * K, d, a);
+        mma_16816(acc[t], a, b0, b1);
+    }
+}
+
 // One GEMV stage of a decoding warp: k-tile rows 4 quad .. 4 quad + 3 of the stage (those below ke)
-// x tiles 4 whalf .. 4 whalf + 3, B fragments of those rows in b. The two words of every tile of the
-// next row are loaded while the current row is decoded, so the shared-memory latency of a row's
-// words overlaps the previous row's arithmetic.
+// x tiles 4 whalf .. 4 whalf + 3, B fragments of those rows in b.
 template <int K>
 __device__ __forceinline__ void gemv_stage(const uint32_t* buf, const LaneW& d, int quad, int whalf, int r0, int ke,
                                            const uint32_t (&b)[2 * WR], float (&acc)[WT][4])
 {
     const uint32_t* rowp = buf + ((WR * quad) * NT + WT * whalf) * 8 * K;
-    const int nr = min(WR, ke - r0);
-    uint32_t w[2][WT][2];
+    if (r0 + WR <= ke) {
 #pragma unroll
-    for (int t = 0; t < WT; ++t) {
-        w[0][t][0] = rowp[t * 8 * K + d.w0];
-        w[0][t][1] = rowp[t * 8 * K + d.w1];
-    }
+        for (int r = 0; r < WR; ++r) gemv_row_w<K>(rowp + r * NT * 8 * K, d, b[2 * r], b[2 * r + 1], acc);
+    } else {
 #pragma unroll
-    for (int r = 0; r < WR; ++r) {
-        if (r >= nr) break;
-        const int cb = r & 1, nb = cb ^ 1;
-        if (r + 1 < WR && r + 1 < nr) {
-#pragma unroll
-            for (int t = 0; t < WT; ++t) {
-                w[nb][t][0] = rowp[(r + 1) * NT * 8 * K + t * 8 * K + d.w0];
-                w[nb][t][1] = rowp[(r + 1) * NT * 8 * K + t * 8 * K + d.w1];
-            }
-        }
-#pragma unroll
-        for (int t = 0; t < WT; ++t) {
-            uint32_t s[8], h[8], a[4];
-            lane_states_w<K, 2>(w[cb][t][0], w[cb][t][1], d, s);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) h[j] = mul1_sum(s[j]);
-            a[0] = __byte_perm(h[0], h[1], 0x5410);
-            a[1] = __byte_perm(h[4], h[5], 0x5410);
-            a[2] = __byte_perm(h[2], h[3], 0x5410);
-            a[3] = __byte_perm(h[6], h[7], 0x5410);
-            mma_16816(acc[t], a, b[2 * r], b[2 * r + 1]);
-        }
+        for (int r = 0; r < WR; ++r)
+            if (r0 + r < ke) gemv_row_w<K>(rowp + r * NT * 8 * K, d, b[2 * r], b[2 * r + 1], acc);
     }
 }
 
@@ -444,11 +431,11 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, co
     uint32_t* ring = reinterpret_cast<uint32_t*>(smem);
     float4* part = reinterpret_cast<float4*>(smem + static_cast<size_t>(NSTAGE) * STAGE_TOTAL);   // [warp][t][lane]
     float* res = reinterpret_cast<float*>(part + PART_F4);                                         // [2][8][128]
-    uint64_t* full = reinterpret_cast<uint64_t*>(res + RES_FLOATS);   // trellis of the stage landed
+    // full: the stage's trellis and B rows landed (arrivals of both producers, with their bytes)
+    uint64_t* full = reinterpret_cast<uint64_t*>(res + RES_FLOATS);
     uint64_t* empty = full + NSTAGE;       // the decoders are done with the stage
     uint64_t* hready = empty + NSTAGE;     // the stage header is written (trellis producer -> B producer)
-    uint64_t* bfull = hready + NSTAGE;     // the stage's B rows landed (or there are none)
-    uint64_t* pfull = bfull + NSTAGE;      // decoders -> epilogue warps: one projection's partial sums written
+    uint64_t* pfull = hready + NSTAGE;     // decoders -> epilogue warps: one projection's partial sums written
     uint64_t* pfree = pfull + 1;           // epilogue warps -> decoders: partial sums consumed
     __shared__ StageHdr hdr[NSTAGE];
     __shared__ PartInfo pinfo;
@@ -460,10 +447,9 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, co
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int i = 0; i < NSTAGE; ++i) {
-            mbar_init(&full[i], 1);
+            mbar_init(&full[i], 2);
             mbar_init(&empty[i], NCW);
             mbar_init(&hready[i], 1);
-            mbar_init(&bfull[i], 1);
         }
         mbar_init(pfull, NCW);
         mbar_init(pfree, NEW);
@@ -560,7 +546,10 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, co
             mbar_wait_sleep(&hready[slot], ph, p.status, 32);
             const int item = hdr[slot].item;
             const int s = hdr[slot].s;
-            if (item < 0) break;
+            if (item < 0) {
+                if (lane == 0) mbar_arrive(&full[slot]);   // the end marker's stage completes without B rows
+                break;
+            }
             if (item != cur_item) {
                 cur_item = item;
                 const WarpItem& hw = hdr[slot].wi;
@@ -578,7 +567,7 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, co
                 __syncwarp();
             }
             if (type != 1 && type != 2) {
-                if (lane == 0) mbar_arrive(&bfull[slot]);
+                if (lane == 0) mbar_arrive(&full[slot]);
                 continue;
             }
             const int proj = type == 2 ? 0 : s / nsp;
@@ -586,11 +575,11 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, co
             const int nvalid = min(STAGE_KT, ke - kt0);
             const __half* brow = type == 1 ? p.xrot + (static_cast<size_t>(proj) * (p.S_cap + p.M) + bslot) * p.hpad
                                            : p.act + static_cast<size_t>(bslot) * p.ipad;
-            if (lane == 0) mbar_arrive_expect_tx(&bfull[slot], nvalid * RUN_ROWS * 32);
+            if (lane == 0) mbar_arrive_expect_tx(&full[slot], nvalid * RUN_ROWS * 32);
             __syncwarp();
             if (lane < RUN_ROWS)
                 bulk_g2s(ring + slot * (STAGE_TOTAL / 4) + (STAGE_BYTES + lane * BROW_BYTES) / 4,
-                         brow + static_cast<size_t>(kt0) * 16, nvalid * 32, &bfull[slot]);
+                         brow + static_cast<size_t>(kt0) * 16, nvalid * 32, &full[slot]);
         }
         return;
     }
@@ -717,7 +706,6 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, co
         const int item = hdr[slot].item;
         const int s = hdr[slot].s;
         if (item < 0) break;
-        mbar_wait(&bfull[slot], ph, p.status);
         const WarpItem& hw = hdr[slot].wi;
         if (item != cur_item) {
             // item start: geometry into registers, the B row, the dependency
