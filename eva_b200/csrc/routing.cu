@@ -12,48 +12,75 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
 namespace eva {
 
 // ---------------------------------------------------------------------------------------------
-// Router logits, small M: one warp per (expert, 512-element k slice); partial sums per slice.
+// Router logits, small M: per 512-element k slice, partial sums of every (token, expert).
+
+// A block takes 32 experts x one 512-element k slice: each warp holds 4 experts' weight slices in
+// registers (16 float4 per lane, all loads in flight at once), the slice of 8 tokens' x at a time is
+// staged in shared memory as FP32, and every (expert, token) partial is a warp reduction.
+constexpr int RG_EXPERTS = 32;
 
 __global__ void __launch_bounds__(256) router_gemv_kernel(const void* __restrict__ x, int x_bf16, int M, int H, int E,
                                                           const float* __restrict__ W, float* __restrict__ part, int KS)
 {
+    __shared__ __align__(16) float xs[8 * ROUTER_KSLICE];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gw = blockIdx.x * 8 + warp;
-    if (gw >= E * KS) return;
-    const int e = gw / KS, ks = gw % KS;
-    const int k0 = ks * ROUTER_KSLICE, k1 = min(H, k0 + ROUTER_KSLICE);
-    const float* wr = W + static_cast<size_t>(e) * H;
+    const int ks = blockIdx.y;
+    const int k0 = ks * ROUTER_KSLICE, klen = min(H - k0, ROUTER_KSLICE);
+    const int eb = blockIdx.x * RG_EXPERTS + warp * 4;
+    float4 w[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int k = lane * 4 + 128 * i;
+            w[j][i] = (eb + j < E && k < klen) ? __ldg(reinterpret_cast<const float4*>(W + static_cast<size_t>(eb + j) * H + k0 + k))
+                                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     for (int m0 = 0; m0 < M; m0 += 8) {
-        float acc[8];
+        __syncthreads();
+        for (int v = threadIdx.x; v < 8 * (ROUTER_KSLICE / 4); v += blockDim.x) {
+            const int t = v / (ROUTER_KSLICE / 4), k = (v % (ROUTER_KSLICE / 4)) * 4;
+            float xv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (m0 + t < M && k < klen) load4_x(x, static_cast<size_t>(m0 + t) * H + k0 + k, x_bf16, xv);
+            *reinterpret_cast<float4*>(xs + t * ROUTER_KSLICE + k) = make_float4(xv[0], xv[1], xv[2], xv[3]);
+        }
+        __syncthreads();
+        float acc[4][8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-        for (int k = k0 + lane * 4; k < k1; k += 128) {
-            const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr + k));
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (m0 + i < M) {
-                    float xv[4];
-                    load4_x(x, static_cast<size_t>(m0 + i) * H + k, x_bf16, xv);
-                    acc[i] = fmaf(w4.x, xv[0], acc[i]);
-                    acc[i] = fmaf(w4.y, xv[1], acc[i]);
-                    acc[i] = fmaf(w4.z, xv[2], acc[i]);
-                    acc[i] = fmaf(w4.w, xv[3], acc[i]);
+            for (int t = 0; t < 8; ++t) acc[j][t] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                const float4 xv = *reinterpret_cast<const float4*>(xs + t * ROUTER_KSLICE + lane * 4 + 128 * i);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    acc[j][t] = fmaf(w[j][i].x, xv.x, acc[j][t]);
+                    acc[j][t] = fmaf(w[j][i].y, xv.y, acc[j][t]);
+                    acc[j][t] = fmaf(w[j][i].z, xv.z, acc[j][t]);
+                    acc[j][t] = fmaf(w[j][i].w, xv.w, acc[j][t]);
                 }
             }
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            float v = acc[i];
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && m0 + i < M) part[(static_cast<size_t>(ks) * M + m0 + i) * E + e] = v;
-        }
+            for (int t = 0; t < 8; ++t) {
+                float v = acc[j][t];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                if (lane == 0 && m0 + t < M && eb + j < E) part[(static_cast<size_t>(ks) * M + m0 + t) * E + eb + j] = v;
+            }
     }
 }
 
@@ -115,8 +142,7 @@ cudaError_t launch_router_logits(const void* x, int x_bf16, int M, int H, int E,
     if (M < ROUTER_TC_MIN_ROWS) {
         const int KS = (H + ROUTER_KSLICE - 1) / ROUTER_KSLICE;
         *ks_used = KS;
-        const int warps = E * KS;
-        router_gemv_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(x, x_bf16, M, H, E, W, part, KS);
+        router_gemv_kernel<<<dim3((E + RG_EXPERTS - 1) / RG_EXPERTS, KS), 256, 0, stream>>>(x, x_bf16, M, H, E, W, part, KS);
     } else {
         *ks_used = 1;
         dim3 grid((E + 63) / 64, (M + 63) / 64);
@@ -160,49 +186,58 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i)
     }
 }
 
-constexpr int TOPK_WARPS = 4;
-
-__global__ void __launch_bounds__(TOPK_WARPS * 32) topk_kernel(EvaMoeShape s, const float* __restrict__ part, int KS, int M,
-                                                               const float* __restrict__ bias, float* __restrict__ logits_out,
-                                                               int32_t* __restrict__ idx_out, float* __restrict__ w_out)
+// One block per token: the block sums the slice partials and evaluates the scores (a thread per
+// expert, E <= 1024), then warp 0 does the group-limited selection and the top-k from shared memory.
+__global__ void __launch_bounds__(1024) topk_kernel(EvaMoeShape s, const float* __restrict__ part, int KS, int M,
+                                                    const float* __restrict__ bias, float* __restrict__ logits_out,
+                                                    int32_t* __restrict__ idx_out, float* __restrict__ w_out)
 {
     extern __shared__ float smem_f[];
+    __shared__ float red_f[32];
+    __shared__ double red_d[32];
     const int E = s.n_experts;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m = blockIdx.x * TOPK_WARPS + warp;
-    if (m >= M) return;
-    float* sc = smem_f + warp * 2 * E;   // unbiased scores
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    const int m = blockIdx.x;
+    float* sc = smem_f;                  // unbiased scores
     float* ch = sc + E;                  // selection values
     // logits = sum of the slice partials in slice order
     float lmax = -INFINITY;
-    for (int e = lane; e < E; e += 32) {
+    for (int e = tid; e < E; e += blockDim.x) {
         float l = 0.0f;
         for (int k = 0; k < KS; ++k) l += part[(static_cast<size_t>(k) * M + m) * E + e];
         if (logits_out) logits_out[static_cast<size_t>(m) * E + e] = l;
         sc[e] = l;
         lmax = fmaxf(lmax, l);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-    __syncwarp();
     if (s.router == EVA_ROUTER_SOFTMAX) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+        if (lane == 0) red_f[warp] = lmax;
+        __syncthreads();
+        lmax = red_f[0];
+        for (int i = 1; i < nw; ++i) lmax = fmaxf(lmax, red_f[i]);
         double sum = 0.0;
-        for (int e = lane; e < E; e += 32) sum += exp(static_cast<double>(sc[e]) - static_cast<double>(lmax));
+        for (int e = tid; e < E; e += blockDim.x) sum += exp(static_cast<double>(sc[e]) - static_cast<double>(lmax));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        for (int e = lane; e < E; e += 32) {
+        if (lane == 0) red_d[warp] = sum;
+        __syncthreads();
+        sum = 0.0;
+        for (int i = 0; i < nw; ++i) sum += red_d[i];
+        for (int e = tid; e < E; e += blockDim.x) {
             const float l = sc[e];
             ch[e] = l;   // softmax is monotonic: select on the logits
             sc[e] = static_cast<float>(exp(static_cast<double>(l) - static_cast<double>(lmax)) / sum);
         }
     } else {
-        for (int e = lane; e < E; e += 32) {
+        for (int e = tid; e < E; e += blockDim.x) {
             const float v = score_of(sc[e], s.router);
             sc[e] = v;
             ch[e] = v + (bias ? bias[e] : 0.0f);
         }
     }
-    __syncwarp();
+    __syncthreads();
+    if (warp != 0) return;
     // group-limited selection: keep the topk_group groups with the largest top-2 sums
     if (s.n_group > 1) {
         const int gsz = E / s.n_group;
@@ -278,12 +313,13 @@ __global__ void __launch_bounds__(TOPK_WARPS * 32) topk_kernel(EvaMoeShape s, co
 cudaError_t launch_topk(const EvaMoeShape& s, const float* part, int ks, int M, const float* bias,
                         float* logits_out, int32_t* idx, float* w, cudaStream_t stream)
 {
-    const size_t smem = static_cast<size_t>(TOPK_WARPS) * 2 * s.n_experts * sizeof(float);
+    const size_t smem = static_cast<size_t>(2) * s.n_experts * sizeof(float);
     if (smem > 48 * 1024) {
         cudaError_t e = cudaFuncSetAttribute(topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
-    topk_kernel<<<(M + TOPK_WARPS - 1) / TOPK_WARPS, TOPK_WARPS * 32, smem, stream>>>(s, part, ks, M, bias, logits_out, idx, w);
+    const int threads = std::min(1024, (s.n_experts + 31) / 32 * 32);
+    topk_kernel<<<M, threads, smem, stream>>>(s, part, ks, M, bias, logits_out, idx, w);
     return cudaGetLastError();
 }
 
