@@ -50,7 +50,8 @@ WsLayout ws_layout(const EvaMoeShape& s, int max_rows, bool allow_split, bool ro
     L.asum = take(St * L.nchA * 4);
     L.tstart = take((E + 2) * 4);
     L.pscan = take(permute_scratch_ints(max_rows, static_cast<int>(E)) * 4);
-    L.tmaps = take(static_cast<size_t>(DEC_MAX_CTAS) * DEC_MAP_SETS * 2 * 128);
+    // tensor maps: decode kernel per-CTA item sets, or the tensor-core path's per-expert trellis maps
+    L.tmaps = take(std::max(static_cast<size_t>(DEC_MAX_CTAS) * DEC_MAP_SETS * 2, (E + 1) * 3) * 128);
     L.pxg = take(tensor_core ? St * H * 2 : 0);
     L.pxu = take(tensor_core ? St * H * 2 : 0);
     L.pap = take(tensor_core ? St * L.imax * 2 : 0);

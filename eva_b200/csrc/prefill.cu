@@ -101,6 +101,7 @@ struct PfParams {
     float* out_f32;
     __nv_bfloat16* out_bf16;
     int* status;
+    const CUtensorMap* tmaps;   // [E + 1][3] trellis maps (gate, up, down) per expert, the shared expert last
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -370,8 +371,7 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
 
 struct PfLoop {
     const CUtensorMap* amap[2];
-    const uint8_t* trellis[2];
-    size_t row_stride;       // bytes between k-tile rows of the trellis
+    const CUtensorMap* tmap[2];   // the trellis maps of the projections
     int chunk, dec_valid;
     int nproj, nkb, row0;    // row0: this CTA's first activation row
     uint32_t rank;           // 0 = leader (issues the MMAs)
@@ -411,24 +411,26 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             __syncwarp();
         }
     } else if (warp == CFG::dec + 2) {
-        // trellis producer: own trellis rows, one bulk copy per k-tile row, into the trellis ring,
-        // whose slots the decoders release as soon as they have read them (so the copies run
-        // TSLOTS - 1 decode stages ahead, independent of the MMA)
+        // trellis producer: the stage's 4 KSUB k-tile rows of this CTA's 128 columns as one 2-D
+        // tensor copy (per-row bulk copies throttle the copy engine), into the trellis ring, whose
+        // slots the decoders release as soon as they have read them (so the copies run TSLOTS - 1
+        // decode stages ahead, independent of the MMA)
         uint8_t* tring = ring + CFG::ring_bytes;
+        if (lane == 0 && L.dec_valid)
+            for (int j = 0; j < (L.nproj > 1 ? 2 : 1); ++j) tmap_acquire(L.tmap[j]);
         for (int s = 0; s < total; ++s) {
             const int ts = s % TS;
             mbar_wait(&B.tempty[ts], ((s / TS) & 1) ^ 1, status);
             const int pj = s / L.nkb, kb = s % L.nkb;
             if (lane == 0) {
-                if (L.dec_valid) mbar_arrive_expect_tx(&B.tfull[ts], 4 * KSUB * TROW);
-                else mbar_arrive(&B.tfull[ts]);
+                if (L.dec_valid) {
+                    mbar_arrive_expect_tx(&B.tfull[ts], 4 * KSUB * TROW);
+                    tma_load_2d(tring + ts * CFG::tslot, pj ? L.tmap[1] : L.tmap[0], L.chunk * NT_PF * 4 * K,
+                                kb * 4 * KSUB, &B.tfull[ts]);
+                } else {
+                    mbar_arrive(&B.tfull[ts]);
+                }
             }
-            __syncwarp();
-            if (L.dec_valid && lane < 4 * KSUB)
-                bulk_g2s(tring + ts * CFG::tslot + lane * TROW,
-                         (pj ? L.trellis[1] : L.trellis[0]) + static_cast<size_t>(kb * 4 * KSUB + lane) * L.row_stride +
-                             static_cast<size_t>(L.chunk) * TROW,
-                         TROW, &B.tfull[ts]);
             __syncwarp();
         }
     } else if (warp == 1) {
@@ -634,9 +636,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
     PfLoop L;
     L.amap[0] = &mg;
     L.amap[1] = &mu;
-    L.trellis[0] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 0));
-    L.trellis[1] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 3));
-    L.row_stride = static_cast<size_t>(I_e / 16) * 32 * Ke;
+    L.tmap[0] = p.tmaps + t.e * 3;
+    L.tmap[1] = p.tmaps + t.e * 3 + 1;
     L.chunk = 2 * pc + static_cast<int>(rank);
     L.dec_valid = L.chunk < nch;
     L.nproj = 2;
@@ -726,8 +727,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
 
     PfLoop L;
     L.amap[0] = L.amap[1] = &ma;
-    L.trellis[0] = L.trellis[1] = reinterpret_cast<const uint8_t*>(pf_ptr(p, t, 6));
-    L.row_stride = static_cast<size_t>(p.H / 16) * 32 * Ke;
+    L.tmap[0] = L.tmap[1] = p.tmaps + t.e * 3 + 2;
     L.chunk = 2 * pc + static_cast<int>(rank);
     L.dec_valid = 1;                                       // H is a multiple of 256
     L.nproj = 1;
@@ -765,6 +765,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
         __syncthreads();
     }
     pf_teardown(S, warp, NCOLS);
+}
+
+// ---------------------------------------------------------------------------------------------
+// pf_maps: the trellis tensor maps of every expert (and the shared expert), one warp per expert:
+// the template of its shape with the expert's projection address, published for the tensor-map
+// proxy (the GEMM kernels acquire before their first copy). Unbound experts (address 0) own no tiles.
+
+struct PfMapTemplates {
+    CUtensorMap gu, dn, sgu, sdn;   // routed gate/up (8 k-tile rows per box), down (4), shared gate/up, down
+};
+
+__global__ void __launch_bounds__(32) pf_maps(const PfParams p, const __grid_constant__ PfMapTemplates tm, CUtensorMap* maps)
+{
+    __shared__ __align__(128) CUtensorMap edit[3];
+    const int e = blockIdx.x, lane = threadIdx.x;
+    const bool shared = e == p.n_local;
+    for (int j = 0; j < 3; ++j) {
+        const int row = j == 0 ? 0 : (j == 1 ? 3 : 6);
+        const int64_t addr = shared ? p.sh[row] : p.tables[row][e];
+        const CUtensorMap* t = j < 2 ? (shared ? &tm.sgu : &tm.gu) : (shared ? &tm.sdn : &tm.dn);
+        reinterpret_cast<uint32_t*>(&edit[j])[lane] = reinterpret_cast<const uint32_t*>(t)[lane];
+        __syncwarp();
+        if (lane == 0 && addr != 0 && (addr & 15) == 0) tmap_replace_addr(&edit[j], reinterpret_cast<const void*>(addr));
+        __syncwarp();
+        tmap_copy_release(maps + e * 3 + j, &edit[j]);
+    }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -816,6 +842,21 @@ __device__ __forceinline__ void pf_combine_item(const PfParams& p, int tok, int 
 
 // ---------------------------------------------------------------------------------------------
 // host side
+
+// Trellis [in/16][out/16][16K] int16 of one projection as [in/16][out/16 x 4K] 8-byte elements, box
+// 8 tiles (one 128-column chunk) x rows k-tile rows; base: any 16-byte aligned device address.
+static bool make_trellis_map(CUtensorMap* m, void* base, int in, int out, int K, int rows)
+{
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(out / 16) * 4 * K, static_cast<cuuint64_t>(in / 16)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(out / 16) * 32 * K};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(NT_PF * 4 * K), static_cast<cuuint32_t>(rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
 
 // fp16 [rows][cols] row-major, box 64 x 128, 128B swizzle
 static bool make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols)
@@ -887,6 +928,16 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     p.out_f32 = a.out_f32;
     p.out_bf16 = static_cast<__nv_bfloat16*>(a.out_bf16);
     p.status = reinterpret_cast<int*>(ws + L.status);
+    CUtensorMap* maps = reinterpret_cast<CUtensorMap*>(ws + L.tmaps);
+    p.tmaps = maps;
+
+    PfMapTemplates tmpl;
+    const int ish = p.I_sh ? p.I_sh : p.I;
+    if (!make_trellis_map(&tmpl.gu, ws, p.H, p.I, p.K, 4 * PfGateCfg::ksub) ||
+        !make_trellis_map(&tmpl.dn, ws, p.I, p.H, p.K, 4 * PfDownCfg::ksub) ||
+        !make_trellis_map(&tmpl.sgu, ws, p.H, ish, p.K_sh, 4 * PfGateCfg::ksub) ||
+        !make_trellis_map(&tmpl.sdn, ws, ish, p.H, p.K_sh, 4 * PfDownCfg::ksub))
+        return cudaErrorInvalidValue;
 
     const uint64_t rows = static_cast<uint64_t>(p.S_cap) + p.M;
     CUtensorMap mg, mu, ma;
@@ -910,6 +961,7 @@ cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream)
     if (e != cudaSuccess) return e;
 
     const int small_grid = num_sms() * 8;
+    pf_maps<<<p.n_local + (p.has_shared ? 1 : 0), 32, 0, stream>>>(p, tmpl, maps);
     pf_rotate<<<small_grid, 256, 0, stream>>>(p);
     // tile upper bound: sum over experts of ceil(n_e / T) <= S / T + E, plus the shared tiles
     const int max_tiles = (p.S_cap + PF_TILE_ROWS - 1) / PF_TILE_ROWS + p.n_local +
