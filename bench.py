@@ -65,6 +65,9 @@ def parse():
     ap.add_argument("--stack-layers", type=int, default=58)
     ap.add_argument("--residency", type=float, default=1.0,
                     help="--stack: fraction of each rank's experts resident on the device (misses from pinned host)")
+    ap.add_argument("--staging", default="device", choices=["device", "host"],
+                    help="--stack --residency < 1: device-side expert cache shared by the layers (planned and "
+                         "copied by the device, next layer prefetched) or the host-managed per-layer residency")
     ap.add_argument("--decode-microbench", action="store_true",
                     help="the EXL3 decode loop alone (tiles resident in shared memory): decoded weights per SM clock "
                          "of each decode design, against the rate HBM streaming needs")
@@ -563,23 +566,80 @@ def ep_bench(args, cfg, dev, rank, world, local):
     dist.destroy_process_group()
 
 
+def _dma_h2d_gbs(dev, nbytes=256 << 20):
+    """Pinned host -> device rate of one cudaMemcpyAsync (the copy engine), for context beside the
+    cache's device-side copy kernel."""
+    import torch
+    src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    dst.copy_(src, non_blocking=True)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(4):
+        dst.copy_(src, non_blocking=True)
+    b.record()
+    torch.cuda.synchronize()
+    return 4 * nbytes / (a.elapsed_time(b) * 1e-3) / 1e9
+
+
 def stack_bench(args, cfg, dev, rank, world, local):
     """Config 5: a decode stream of batch --batch per rank through --stack-layers layers, experts
-    sharded over the ranks (EPMoE, peer-memory exchange), optionally only --residency of each rank's
-    experts resident (ExpertResidency: misses copied from pinned host memory on a side stream)."""
+    sharded over the ranks (EPMoE, peer-memory exchange). With --residency r < 1 only r of each rank's
+    experts (over all layers) have device slots: by default one ExpertPool per rank shared by the
+    layers (needed experts planned and copied from pinned host memory by the device, the next layer's
+    predicted experts prefetched on a side stream under the current layer), with --staging host the
+    host-managed per-layer ExpertResidency. The cached run is followed by the same stack fully
+    resident, which gives the exposed staging time (step time difference) and so the fraction of the
+    staging work that ran hidden under compute."""
     import math
     import torch
     import torch.distributed as dist
     from eva_b200.ep import EPMoE, ExpertPlacement
     from eva_b200.experts import make_layer
-    from eva_b200.residency import ExpertResidency
+    from eva_b200.residency import ExpertPool, ExpertResidency
     from eva_b200.stack import MoEStack, make_norms
 
     L, M = args.stack_layers, args.batch
     pl = ExpertPlacement.balanced(zipf_load(cfg), world)
     mine = pl.experts_of(rank)
-    n_slots = max(1, math.ceil(args.residency * len(mine)))
-    if args.residency < 1.0:
+    cached = args.residency < 1.0
+    pooled = cached and args.staging == "device"
+    steps, warmup = args.steps, max(3, args.warmup)
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    xs = torch.randn(steps + warmup, M, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
+    norms = make_norms(L, cfg.hidden, dev, seed=5)
+
+    def run(layers, timed_start=None):
+        stack = MoEStack(layers, norms)
+        for i in range(warmup):
+            stack.forward(xs[i], out=out)
+        torch.cuda.synchronize()
+        if timed_start is not None:
+            timed_start()
+        if world > 1:
+            dist.barrier()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        t0.record()
+        for i in range(steps):
+            stack.forward(xs[warmup + i], out=out)
+        t1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - w0
+        st = 0
+        for lay in layers:
+            st |= lay.status()
+        return t0.elapsed_time(t1), wall, st
+
+    def made(li):
+        lay = make_layer(cfg, dev, seed=1000 + li, experts=mine)
+        return dataclasses_replace(lay, router_b=zipf_bias(cfg, lay.router_b))
+
+    t_build = time.perf_counter()
+    hosts, stats = [], None
+    if cached:
         # every rank pins its experts of every layer in host memory: refuse rather than exhaust it
         rec = 3 * cfg.hidden * cfg.inter * cfg.bits // 8 + 6 * (cfg.hidden + cfg.inter)
         need = L * len(mine) * (rec + 4096) * int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
@@ -587,54 +647,90 @@ def stack_bench(args, cfg, dev, rank, world, local):
         if need > 0.7 * avail:
             raise SystemExit(f"--residency {args.residency}: {need / 2**30:.0f} GiB of pinned host memory over the "
                              f"node's ranks, {avail / 2**30:.0f} GiB available; use fewer --stack-layers")
-    layers, residencies = [], []
-    t_build = time.perf_counter()
-    for li in range(L):
-        lay = make_layer(cfg, dev, seed=1000 + li, experts=mine)
-        lay = dataclasses_replace(lay, router_b=zipf_bias(cfg, lay.router_b))
-        if args.residency < 1.0:
-            host = lay.host_copy()
+        for li in range(L):
+            lay = made(li)
+            hosts.append(lay.host_copy(pinned=True))
             del lay
-            res = ExpertResidency(host, n_slots, dev)
-            residencies.append(res)
-            layers.append(EPMoE(host, pl, max_tokens=M, residency=res))
+        if pooled:
+            n_slots = max(len(mine), math.ceil(args.residency * L * len(mine)))
+            pool = ExpertPool(dev, n_slots, hosts[0].record_bytes, max_layers=L, timing=True)
+            pls = [pool.add_layer(h) for h in hosts]
+            for li in range(L):
+                pls[li].next = pls[(li + 1) % L]     # the last layer prefetches the next step's first
+            layers = [EPMoE(h, pl, max_tokens=M, residency=r) for h, r in zip(hosts, pls)]
         else:
-            layers.append(EPMoE(lay, pl, max_tokens=M))
-    norms = make_norms(L, cfg.hidden, dev, seed=5)
-    stack = MoEStack(layers, norms)
+            n_slots = max(1, math.ceil(args.residency * len(mine)))
+            residencies = [ExpertResidency(h, n_slots, dev) for h in hosts]
+            layers = [EPMoE(h, pl, max_tokens=M, residency=r) for h, r in zip(hosts, residencies)]
+    else:
+        layers = [EPMoE(made(li), pl, max_tokens=M) for li in range(L)]
     t_build = time.perf_counter() - t_build
-    steps, warmup = args.steps, max(3, args.warmup)
-    g = torch.Generator(device=dev)
-    g.manual_seed(7 + rank)
-    xs = torch.randn(steps + warmup, M, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
-    out = torch.empty(M, cfg.hidden, dtype=torch.bfloat16, device=dev)
-    for i in range(warmup):
-        stack.forward(xs[i], out=out)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    for r in residencies:
-        r.stats.update(hits=0, misses=0, h2d_bytes=0)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    w0 = time.perf_counter()
-    t0.record()
-    for i in range(steps):
-        stack.forward(xs[warmup + i], out=out)
-    t1.record()
-    torch.cuda.synchronize()
-    wall = time.perf_counter() - w0
-    ms = t0.elapsed_time(t1)
+
+    b0 = [0]
+
+    def timed_start():      # counters cover the timed steps only
+        if pooled:
+            b0[0] = pool.bytes_copied()
+            pool.staging_ms()
+        elif cached:
+            for r in residencies:
+                r.stats.update(hits=0, misses=0, h2d_bytes=0)
+
+    ms, wall, st = run(layers, timed_start)
+    resident_ms = None
+    if pooled:
+        h2d = pool.bytes_copied() - b0[0]
+        stg = pool.staging_ms()
+        st |= pool.status()
+        stats = {"kind": "device expert cache (ExpertPool): one pool per GPU shared by the layers",
+                 "slots_per_gpu": n_slots, "slots_per_gpu_if_resident": L * len(mine),
+                 "h2d_bytes_per_step": h2d / steps,
+                 "plan_ms_per_step": stg["plan"] / steps,
+                 "miss_copy_ms_per_step": stg["copy"] / steps,
+                 "prefetch_ms_per_step": stg["prefetch"] / steps,
+                 "h2d_gbs_of_copy_launches": h2d / max(1e-9, stg["copy"] + stg["prefetch"]) / 1e6,
+                 "h2d_gbs_copy_engine_256mb": _dma_h2d_gbs(dev)}
+    elif cached:
+        h2d = sum(r.stats["h2d_bytes"] for r in residencies)
+        stats = {"kind": "host-managed per-layer residency (ExpertResidency)", "slots_per_layer": n_slots,
+                 "h2d_bytes_per_step": h2d / steps, "misses": sum(r.stats["misses"] for r in residencies),
+                 "hits": sum(r.stats["hits"] for r in residencies)}
+    if cached:
+        # the same stack with every expert resident (if the device holds it): exposed staging time
+        for lay in layers:
+            lay.close()
+        del layers
+        if pooled:
+            del pls, pool
+        else:
+            del residencies
+        torch.cuda.empty_cache()
+        full_bytes = L * sum(h.storage.numel() for h in hosts[:1])
+        fits = full_bytes < 0.8 * torch.cuda.mem_get_info(dev)[0]
+        if world > 1:
+            fits = _max_over_ranks(0 if fits else 1, dev) == 0
+        if fits:
+            layers = [EPMoE(h.to(dev), pl, max_tokens=M) for h in hosts]
+            resident_ms, _, st_r = run(layers)
+            st |= st_r
     if world > 1:
         ms = _max_over_ranks(ms, dev)
-    st = 0
-    for lay in layers:
-        st |= lay.status()
-    h2d = sum(r.stats["h2d_bytes"] for r in residencies)
-    misses = sum(r.stats["misses"] for r in residencies)
-    hits = sum(r.stats["hits"] for r in residencies)
-    if world > 1:
         st = int(_max_over_ranks(st, dev))
-        h2d = _max_over_ranks(h2d, dev)
+        if resident_ms is not None:
+            resident_ms = _max_over_ranks(resident_ms, dev)
+        if stats is not None:
+            for k in [k for k in stats if k.startswith(("h2d", "plan", "miss", "prefetch"))]:
+                stats[k] = _max_over_ranks(stats[k], dev)
+    if stats is not None:
+        stats["resident_ms_per_step"] = None if resident_ms is None else resident_ms / steps
+        if resident_ms is not None:
+            exposed = max(0.0, (ms - resident_ms) / steps)
+            stats["exposed_staging_ms_per_step"] = exposed
+            if pooled:
+                total = sum(stats[k] for k in ("plan_ms_per_step", "miss_copy_ms_per_step", "prefetch_ms_per_step"))
+                stats["staging_hidden_fraction"] = None if total <= 0 else max(0.0, 1.0 - exposed / total)
+        stats["note"] = ("max over ranks; exposed = cached minus resident step time; hidden fraction = 1 - exposed / "
+                         "device time of all staging launches (plans, miss copies, prefetches)")
     line = {"metric": "moe_stack_decode_tokens_per_s", "value": M * world * steps / (ms * 1e-3), "unit": UNIT,
             "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16 (EXL3 K3), bf16 in/out, fp32 residual",
@@ -643,10 +739,9 @@ def stack_bench(args, cfg, dev, rank, world, local):
                                    f"attention stubbed, decode batch {M} tokens/step per GPU, expert parallel over "
                                    f"{world} GPUs", "layers": L, "batch": M, "global_batch": M * world,
                        "experts_per_gpu_per_layer": len(mine), "residency": args.residency,
-                       "device_slots_per_layer": n_slots if residencies else len(mine),
+                       "staging": args.staging if cached else None,
                        "parallelism": f"ep{world}", "exchange": EXCHANGE["peers"]},
-            "residency_stats": {"h2d_bytes_per_step_max_rank": h2d / steps, "misses": misses, "hits": hits}
-                               if residencies else None,
+            "residency_stats": stats,
             "wall_ms_per_step": 1e3 * wall / steps, "build_s": t_build, "device_status": st}
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -23,7 +23,7 @@ EXPORTS = ("eva_moe_workspace_bytes", "eva_moe_clear_status", "eva_moe_read_stat
            "eva_ep_dispatch", "eva_ep_combine", "eva_ep_arena_layout", "eva_peer_alloc", "eva_peer_open",
            "eva_peer_close", "eva_peer_free", "eva_ep_dispatch_peers", "eva_ep_wait_rows", "eva_ep_signal_partials",
            "eva_ep_combine_peers", "eva_rmsnorm_residual", "eva_moe_experts_window", "eva_decode_microbench",
-           "eva_tc_selftest")
+           "eva_tc_selftest", "eva_pool_plan", "eva_pool_copy", "eva_host_mapped")
 EP_MAX_WORLD = 32
 NOALLOC_SCRATCH_BYTES = 16 << 20
 
@@ -43,6 +43,18 @@ def shape_of(cfg: MoEConfig, *, shared: bool = True, bits: int | None = None, li
                        cfg.bits if bits is None else bits, cfg.shared_inter if shared else 0, cfg.shared_bits,
                        cfg.router_code, cfg.n_group, cfg.topk_group, int(cfg.norm_topk), act_routed, act_shared,
                        float(cfg.route_scale), float(cfg.swiglu_limit if limit is None else limit))
+
+
+class EvaExpertPool(ctypes.Structure):
+    _fields_ = [("n_slots", ctypes.c_int32), ("reserved", ctypes.c_int32), ("record_bytes", ctypes.c_int64),
+                ("slots", ctypes.c_void_p), ("owner", ctypes.c_void_p), ("stamp", ctypes.c_void_p),
+                ("state", ctypes.c_void_p)]
+
+
+class EvaPoolLayer(ctypes.Structure):
+    _fields_ = [("layer", ctypes.c_int32), ("n_local", ctypes.c_int32), ("host_records", ctypes.c_void_p),
+                ("row_off", ctypes.c_int64 * 9), ("slot_of", ctypes.c_void_p), ("last_needed", ctypes.c_void_p),
+                ("table", ctypes.c_void_p)]
 
 
 class EvaEpPeers(ctypes.Structure):
@@ -118,6 +130,12 @@ def load(build_if_missing: bool = True):
     L.eva_decode_microbench.argtypes = [i32, i32, i32, P(ctypes.c_double), vp]
     L.eva_tc_selftest.restype = ctypes.c_int
     L.eva_tc_selftest.argtypes = [i32, vp, vp, vp, vp, vp]
+    L.eva_pool_plan.restype = ctypes.c_int
+    L.eva_pool_plan.argtypes = [P(EvaExpertPool), vp, i32, vp, i32, vp, i32, i32, i32, vp, vp, vp, vp]
+    L.eva_pool_copy.restype = ctypes.c_int
+    L.eva_pool_copy.argtypes = [P(EvaExpertPool), vp, i32, vp, vp]
+    L.eva_host_mapped.restype = ctypes.c_int
+    L.eva_host_mapped.argtypes = [vp]
     L.eva_moe_arch.restype = i32
     L.eva_moe_arch.argtypes = []
     _lib = L

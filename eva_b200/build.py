@@ -15,7 +15,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libeva_moe.so"
 SOURCES = ["capi.cu", "routing.cu", "router_tc.cu", "experts.cu", "prefill.cu", "noalloc.cu", "ep.cu", "stack.cu",
-           "decode_bench.cu"]
+           "decode_bench.cu", "residency.cu"]
 HEADERS = ["common.cuh", "internal.h", "tc.cuh", "decode_tc.cuh"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

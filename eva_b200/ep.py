@@ -115,6 +115,7 @@ class CudaEpOps:
         self.lib = _lib.load()
         self.cfg, self.layer, self.device = cfg, layer, device
         self.residency = residency
+        self._miss_part = None          # partial rows of the copied experts' launch (expert cache)
         self.router_w = layer.router_w.to(device)
         self.router_b = layer.router_b.to(device)
         self.world = placement.world
@@ -289,15 +290,30 @@ class CudaEpOps:
     def experts_arena(self, own_rows: int = -1):
         """Routed experts of every received row, from this rank's arena into its partial rows.
 
-        With expert residency, the experts the received rows select are made resident first (misses
-        copied from pinned host memory on the side stream); when more are selected than there are
-        slots, they run in groups that fit, each group's slots masked into its own launch and the
-        partial sums added."""
+        With a PooledLayer (device-side expert cache), the experts the received rows select are made
+        resident on the device stream without a host synchronisation, and the next layer's prefetch is
+        issued. With an ExpertResidency (host-managed), the needed set is read on the host (a
+        synchronisation), misses are copied from pinned host memory on the side stream, and when more
+        are selected than there are slots they run in groups that fit, each group's slots masked into
+        its own launch and the partial sums added."""
         P = self.peers
         base = self._own_arena
         res = self.residency
         if res is None:
             self._experts_call(base + P.off_rw, base + P.off_part, own_rows)
+        elif hasattr(res, "plan"):
+            # device-side expert cache: the plan in stream order; the misses' copies, then the next
+            # layer's prefetch, on the pool's copy stream; the resident experts' launch overlaps the
+            # copies and the copied experts' launch follows them
+            hit, miss, copied = res.plan(self.recv_sel, self.recv_rw, split=True)
+            if res.next is not None:
+                res.next.prefetch()
+            self._experts_call(hit.data_ptr(), base + P.off_part, own_rows)
+            torch.cuda.current_stream(self.device).wait_event(copied)
+            if self._miss_part is None:
+                self._miss_part = torch.empty_like(self.part)
+            self._experts_call(miss.data_ptr(), self._miss_part.data_ptr(), -1)
+            self.part.add_(self._miss_part)
         else:
             active = self.recv_rw != 0
             needed = torch.unique(self.recv_sel[active]).tolist()      # host synchronisation

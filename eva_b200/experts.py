@@ -92,9 +92,14 @@ class ExpertLayer:
             return raw.view(torch.int16).view(fin // 16, fout // 16, 16 * bits)
         return raw.view(torch.float16)
 
-    def host_copy(self) -> "ExpertLayer":
-        """Same experts in host memory (pointer tables re-based), for the CPU oracle."""
-        storage = self.storage.cpu()
+    def host_copy(self, pinned: bool = False) -> "ExpertLayer":
+        """Same experts in host memory (pointer tables re-based): for the CPU oracle, or page-locked
+        (pinned=True) as the host side of an expert cache."""
+        if pinned:
+            storage = torch.empty(self.storage.numel(), dtype=torch.uint8, pin_memory=True)
+            storage.copy_(self.storage)
+        else:
+            storage = self.storage.cpu()
         return _with_storage(self, storage)
 
     def to(self, device) -> "ExpertLayer":

@@ -285,6 +285,63 @@ int eva_rmsnorm_residual(int32_t H, int32_t M, float* resid, const float* add, c
 /* Library identification: sm arch the kernels were built for (100 for sm_100a). */
 int32_t eva_moe_arch(void);
 
+/* ---- device-side expert cache (rows of the reference's ExpertCache: cache.py:1852-2080) --------
+ * A pool of device record slots shared by every layer on the GPU. Replaces _install_if_absent /
+ * _blit / _bind / _unbind / _flush and prefetch_gpu (runtime/ds41/cache.py:1852-1996, 2064-2080) and
+ * the host sync on the routes that decides what to install (cache.py:2315): the needed set, the slot
+ * choice (CLOCK, free slots first, slots in use by the running or the planned layer protected) and
+ * the pointer-table updates run on the device; copies read the pinned host records by their unified
+ * addresses. Nothing synchronises the host.
+ *
+ * EvaExpertPool (device arrays): slots n_slots * record_bytes; owner [n_slots] (layer << 16 | expert,
+ *   -1 free); stamp [n_slots]; state int32 [6] = {hand, plan counter, status bits, 0, bytes copied
+ *   (int64)}, zero-initialised with owner = -1.
+ * EvaPoolLayer (one per layer, an array of them in device memory): layer's n_local (<= 1024) experts;
+ *   host_records: pinned host memory, n_local records of record_bytes; row_off: byte offsets of the 9
+ *   tensors inside a record (handle row order); slot_of [n_local] (-1 = not resident); last_needed:
+ *   bitmap of the last exact plan (what a prefetch predicts); table: the layer's int64 [9][n_local]
+ *   pointer-table handle, kept bound to the resident copies (0 = not resident).
+ *
+ * eva_pool_plan: exact (prefetch = 0): the experts selected by rows x topk routes (rw != 0) of layer
+ *   `layer` become resident (misses get slots; their copy jobs go to jobs = {n, (expert, slot) x n});
+ *   prefetch (prefetch = 1): the same for the layer's last exact needed set, issued while another
+ *   layer runs (that layer's slots are protected; best effort: it stops when no slot is free). Status
+ *   bit EVA_STATUS_CAPACITY in state[2] when the pool cannot hold a layer's needed set; the routes of
+ *   the experts left without a slot then get weight 0 (in rw itself when rw_hit is NULL), so that no
+ *   launch reads an unbound expert. rw_hit / rw_miss (optional, device float [rows x topk], exact
+ *   plans only): rw split into the routes of experts already resident and of those being copied, so
+ *   that one experts launch over rw_hit can overlap the copies and a second one over rw_miss follows
+ *   them. jobs: device int32 [1 + 2 n_local].
+ * eva_pool_copy: copies the jobs of the last plan of `layer` (stream order after the plan). */
+typedef struct {
+    int32_t n_slots;
+    int32_t reserved;
+    int64_t record_bytes;
+    void* slots;
+    int32_t* owner;
+    int32_t* stamp;
+    int32_t* state;
+} EvaExpertPool;
+
+typedef struct {
+    int32_t layer, n_local;
+    const void* host_records;
+    int64_t row_off[9];
+    int32_t* slot_of;
+    uint32_t* last_needed;
+    int64_t* table;
+} EvaPoolLayer;
+
+int eva_pool_plan(const EvaExpertPool* pool, const EvaPoolLayer* layers, int32_t layer, const void* sel,
+                  int32_t sel_is_i64, float* rw, int32_t rows, int32_t topk, int32_t prefetch, int32_t* jobs,
+                  float* rw_hit, float* rw_miss, void* stream);
+int eva_pool_copy(const EvaExpertPool* pool, const EvaPoolLayer* layers, int32_t layer, const int32_t* jobs,
+                  void* stream);
+
+/* 1 when p is pinned host memory that kernels can read at the same address (unified addressing), else 0.
+ * Callers of eva_pool_copy check their host records with it. */
+int eva_host_mapped(const void* p);
+
 /* ---- measurement and self-test entry points (no counterpart in the reference) ----------------
  *
  * eva_decode_microbench: the EXL3 decode loop alone, on trellis tiles resident in shared memory (no
