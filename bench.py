@@ -404,6 +404,47 @@ def _max_over_ranks(v, dev):
     return float(t.item())
 
 
+def _max_min_over_ranks(vals, dev):
+    """Element-wise (max, min) over ranks of a list of floats."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(vals, dtype=torch.float64, device=dev)
+    hi, lo = t.clone(), -t
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+    dist.all_reduce(lo, op=dist.ReduceOp.MAX)
+    return hi.tolist(), (-lo).tolist()
+
+
+def _phase_split(ep, inputs, n, dev, **kw):
+    """Per-phase device time of n extra EP steps (after the timed ones), mean ms per step on each rank,
+    as {phase: {"max_rank": ms, "min_rank": ms}}: which phase the step time goes to, and how unevenly
+    (wait = until every peer's rows arrived, combine = until every peer's partials arrived + the sum)."""
+    import torch
+    runs = []
+    for i in range(n):
+        ph = []
+        ep.forward(inputs[i % len(inputs)], phases=ph, **kw)
+        runs.append(ph)
+    torch.cuda.synchronize()
+    names = [nm for nm, _ in runs[0][1:]]
+    mean = [statistics.mean(r[j][1].elapsed_time(r[j + 1][1]) for r in runs) for j in range(len(names))]
+    hi, lo = _max_min_over_ranks(mean, dev)
+    return {nm: {"max_rank": h, "min_rank": l} for nm, h, l in zip(names, hi, lo)}
+
+
+def _placement_balance(allidx, owner, world):
+    """Routed (token, k) slots and distinct experts per rank per step, from the gathered routes
+    [steps, world, M, k]: max / min over ranks of the per-step means."""
+    import torch
+    own = owner[allidx]                                     # [steps, world, M, k] owning rank
+    slots = [float((own == r).sum()) / allidx.shape[0] for r in range(world)]
+    distinct = [statistics.mean(int((owner[allidx[i].unique()] == r).sum()) for i in range(allidx.shape[0]))
+                for r in range(world)]
+    return {"slots_per_step_max_rank": max(slots), "slots_per_step_min_rank": min(slots),
+            "slots_max_over_mean": max(slots) / max(1e-9, statistics.mean(slots)),
+            "distinct_experts_per_step_max_rank": max(distinct), "distinct_experts_per_step_min_rank": min(distinct)}
+
+
 def ep_bench(args, cfg, dev, rank, world, local):
     """N > 1: expert parallelism. Each rank holds n_experts / N experts (placed by expected load) and
     its own batch of tokens (weak scaling); the step is EPMoE.forward: route, dispatch, NCCL
@@ -484,6 +525,9 @@ def ep_bench(args, cfg, dev, rank, world, local):
             clock_summary = dict(clocks.summary(), note="timed region shorter than the 50 ms sampling period; "
                                                         "samples from warm-up through e2e")
         st = int(_max_over_ranks(st, dev))
+        phases = (_phase_split(ep, [xs[warmup + i] for i in range(steps)], min(steps, 20), dev, out=out)
+                  if args.ep_transport == "peers" else None)
+        balance = _placement_balance(allidx[warmup:], owner, world)
         peak, peak_kind = peaks()
         tokens = M * steps * world
         line = {
@@ -511,6 +555,10 @@ def ep_bench(args, cfg, dev, rank, world, local):
             "gpu_launches": (12 if args.ep_transport == "peers" else 9) * steps,
             "clocks": clock_summary,
             "device_status": st,
+            "phase_ms_per_step": phases,
+            "placement_balance": balance,
+            "rank_evidence": "the peer-memory exchange makes no NCCL calls on the step (NCCL only for setup "
+                             "and the max-over-ranks reductions): N busy GPUs show the ranks",
         }
         ep.close()
         del ep, xs
@@ -539,6 +587,11 @@ def ep_bench(args, cfg, dev, rank, world, local):
         torch.cuda.synchronize()
         pms = _max_over_ranks(t0.elapsed_time(t1) / psteps, dev)
         pst = int(_max_over_ranks(ep.status(), dev))
+        pphases = _phase_split(ep, xs, 4, dev, out=out) if args.ep_transport == "peers" else None
+        ep.forward(xs[0], out=out, idx_out=idx)
+        gathered = [torch.empty_like(idx) for _ in range(world)]
+        dist.all_gather(gathered, idx)
+        pbalance = _placement_balance(torch.stack(gathered, 0)[None].cpu().to(torch.int64), owner, world)
         flop = 6.0 * cfg.hidden * (P * world * cfg.topk * cfg.inter + P * world * cfg.shared_inter)
         peak, kind = tensor_peak()
         achieved = flop / world / (pms * 1e-3) / 1e12
@@ -552,7 +605,8 @@ def ep_bench(args, cfg, dev, rank, world, local):
                                "all-to-all of FP32 partial sums back",
                    "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                                 "frac": achieved / peak, "peak_kind": kind,
-                                "kernel": "whole EP prefill step per rank (routed + shared expert FLOPs / N)"}}
+                                "kernel": "whole EP prefill step per rank (routed + shared expert FLOPs / N)"},
+                   "phase_ms_per_step": pphases, "placement_balance": pbalance}
         ep.close()
         del ep
         torch.cuda.empty_cache()

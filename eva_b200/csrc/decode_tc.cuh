@@ -87,14 +87,14 @@ __device__ __forceinline__ void lane_states_w(uint32_t w0, uint32_t w1, const La
     }
 }
 
-// A fragment of mma.m16n8k16 (weights as A[m = n][k]) for one tile: raw codebook values
+// A fragment of mma.m16n8k16 (weights as A[m = n][k]) for one tile, from the lane's two words: raw codebook values
 // h = 1024 + bytesum as exact fp16 pairs, reg0 (g; 2t, 2t+1) reg1 (g+8; 2t, 2t+1) reg2 (g; 2t+8, 2t+9)
 // reg3 (g+8; 2t+8, 2t+9). PRMT: pack pairs with a byte permute (ALU) instead of a multiply-add (FMA).
 template <int K, int NB, bool PRMT>
-__device__ __forceinline__ void decode_afrag_w(const uint32_t* tile, const LaneW& d, uint32_t (&a)[4])
+__device__ __forceinline__ void decode_afrag_ww(uint32_t w0, uint32_t w1, const LaneW& d, uint32_t (&a)[4])
 {
     uint32_t s[8];
-    lane_states_w<K, NB>(tile[d.w0], tile[d.w1], d, s);
+    lane_states_w<K, NB>(w0, w1, d, s);
     uint32_t h[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) h[j] = mul1_sum(s[j]);
@@ -109,6 +109,13 @@ __device__ __forceinline__ void decode_afrag_w(const uint32_t* tile, const LaneW
         a[2] = imad_pack(h[3], h[2]);
         a[3] = imad_pack(h[7], h[6]);
     }
+}
+
+// The same from the tile in shared memory (words d.w0, d.w1).
+template <int K, int NB, bool PRMT>
+__device__ __forceinline__ void decode_afrag_w(const uint32_t* tile, const LaneW& d, uint32_t (&a)[4])
+{
+    decode_afrag_ww<K, NB, PRMT>(tile[d.w0], tile[d.w1], d, a);
 }
 
 // i8 form: the eight mul1 products in 16x256b.x2 register order

@@ -130,6 +130,20 @@ __global__ void __launch_bounds__(EP_PLAN_THREADS) ep_plan_kernel(EpDispatchArgs
     }
 }
 
+// One warp copies a row, 4 loads in flight per lane.
+__device__ __forceinline__ void copy_row_warp(const uint4* src, uint4* dst, size_t n16, int lane)
+{
+    for (size_t i = lane; i < n16; i += 4 * 32) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (i + u * 32 < n16) v[u] = __ldcs(src + i + u * 32);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (i + u * 32 < n16) dst[i + u * 32] = v[u];
+    }
+}
+
 // Warp per (token, destination): copy the x row and write the destination-local slot metadata.
 // With fixed segments, warps past the tokens zero the padding rows' metadata.
 __global__ void __launch_bounds__(256) ep_pack_kernel(EpDispatchArgs a)
@@ -144,7 +158,7 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(EpDispatchArgs a)
         if (p < 0) return;
         const uint4* src = reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(m) * row_bytes);
         uint4* dst = reinterpret_cast<uint4*>(a.send_x + static_cast<size_t>(p) * row_bytes);
-        for (size_t i = lane; i < row_bytes / 16; i += 32) dst[i] = __ldcs(src + i);
+        copy_row_warp(src, dst, row_bytes / 16, lane);
         for (int j = lane; j < a.topk; j += 32) {
             const int d = slot_dest(a, m, j, false);
             const bool on = d == r;
@@ -275,48 +289,66 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v)
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Warp per (token, destination) row, then per padding row; the last block to finish releases the
-// "rows ready" flag of this source at every destination.
-__global__ void __launch_bounds__(256) ep_pack_peers_kernel(EpDispatchArgs a, EvaEpPeers P)
+// Block per (token, destination) row (its threads copy the row with 4 loads in flight each), then
+// blocks of 8 padding rows (warp per row); the last block to finish releases the "rows ready" flag of
+// this source at every destination.
+constexpr int PACK_THREADS = 256;
+constexpr int PACK_PAD_ROWS = PACK_THREADS / 32;
+
+__global__ void __launch_bounds__(PACK_THREADS) ep_pack_peers_kernel(EpDispatchArgs a, EvaEpPeers P)
 {
     const int lane = threadIdx.x & 31;
-    const long long gw = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const long long n_pairs = static_cast<long long>(a.M) * a.world;
     const size_t row_bytes = static_cast<size_t>(a.H) * a.elem_bytes;
     const int seg = a.segment, k = a.topk;
-    if (gw < n_pairs) {
-        const int m = static_cast<int>(gw / a.world), r = static_cast<int>(gw % a.world);
+    if (blockIdx.x < n_pairs) {
+        const int m = static_cast<int>(blockIdx.x / a.world), r = static_cast<int>(blockIdx.x % a.world);
         const int p = a.pos[static_cast<size_t>(r) * a.M + m];
         if (p >= 0) {
             const size_t row = static_cast<size_t>(P.rank) * seg + p;
             uint8_t* dst = arena_of(P, r);
             const uint4* src = reinterpret_cast<const uint4*>(a.x + static_cast<size_t>(m) * row_bytes);
             uint4* dx = reinterpret_cast<uint4*>(dst + P.off_x + row * row_bytes);
-            for (size_t i = lane; i < row_bytes / 16; i += 32) dx[i] = __ldcs(src + i);
-            int32_t* ds = reinterpret_cast<int32_t*>(dst + P.off_sel) + row * k;
-            float* dw = reinterpret_cast<float*>(dst + P.off_rw) + row * k;
-            for (int j = lane; j < k; j += 32) {
-                const int d = slot_dest(a, m, j, false);
-                const int s = m * k + j;
-                ds[j] = d == r ? a.local_id[a.idx[s]] : 0;
-                dw[j] = d == r ? a.w[s] : 0.0f;
+            const size_t n16 = row_bytes / 16;
+            for (size_t i = threadIdx.x; i < n16; i += 4 * PACK_THREADS) {
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (i + u * PACK_THREADS < n16) v[u] = __ldcs(src + i + u * PACK_THREADS);
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    if (i + u * PACK_THREADS < n16) dx[i + u * PACK_THREADS] = v[u];
+            }
+            if (threadIdx.x < 32) {
+                int32_t* ds = reinterpret_cast<int32_t*>(dst + P.off_sel) + row * k;
+                float* dw = reinterpret_cast<float*>(dst + P.off_rw) + row * k;
+                for (int j = lane; j < k; j += 32) {
+                    const int d = slot_dest(a, m, j, false);
+                    const int s = m * k + j;
+                    ds[j] = d == r ? a.local_id[a.idx[s]] : 0;
+                    dw[j] = d == r ? a.w[s] : 0.0f;
+                }
             }
         }
-    } else if (gw - n_pairs < static_cast<long long>(a.world) * seg) {
-        const long long q = gw - n_pairs;
-        const int r = static_cast<int>(q / seg), i = static_cast<int>(q % seg);
-        if (i >= a.counts[r]) {
-            uint8_t* dst = arena_of(P, r);
-            const size_t row = static_cast<size_t>(P.rank) * seg + i;
-            for (int j = lane; j < k; j += 32) {
-                reinterpret_cast<int32_t*>(dst + P.off_sel)[row * k + j] = 0;
-                reinterpret_cast<float*>(dst + P.off_rw)[row * k + j] = 0.0f;
+    } else {
+        const long long q = (blockIdx.x - n_pairs) * PACK_PAD_ROWS + (threadIdx.x >> 5);
+        if (q < static_cast<long long>(a.world) * seg) {
+            const int r = static_cast<int>(q / seg), i = static_cast<int>(q % seg);
+            if (i >= a.counts[r]) {
+                uint8_t* dst = arena_of(P, r);
+                const size_t row = static_cast<size_t>(P.rank) * seg + i;
+                for (int j = lane; j < k; j += 32) {
+                    reinterpret_cast<int32_t*>(dst + P.off_sel)[row * k + j] = 0;
+                    reinterpret_cast<float*>(dst + P.off_rw)[row * k + j] = 0.0f;
+                }
             }
         }
     }
-    __threadfence_system();
+    // the block's stores are ordered before thread 0's system-scope fence by the barrier (one fence
+    // per block instead of one per thread), and the fence before its counter increment
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence_system();
         uint32_t* ctr = flag_at(P, P.rank, FLAG_CTR);
         const uint32_t prev = atomicAdd(ctr, 1u);
         if (prev == gridDim.x - 1) {
@@ -471,10 +503,10 @@ extern "C" int eva_ep_dispatch_peers(const EvaEpPeers* p, const void* x, int32_t
                      all_to_self ? p->rank : -1};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     ep_plan_kernel<<<1, EP_PLAN_THREADS, 0, s>>>(a);
-    const long long warps = static_cast<long long>(M) * p->world + static_cast<long long>(p->world) * p->segment_rows;
-    const long long blocks = (warps * 32 + 255) / 256;
+    const long long pad_rows = static_cast<long long>(p->world) * p->segment_rows;
+    const long long blocks = static_cast<long long>(M) * p->world + (pad_rows + PACK_PAD_ROWS - 1) / PACK_PAD_ROWS;
     if (blocks > 0x7fffffffLL) return EVA_ERR_INVALID;
-    ep_pack_peers_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(a, *p);
+    ep_pack_peers_kernel<<<static_cast<unsigned>(blocks), PACK_THREADS, 0, s>>>(a, *p);
     return cudaGetLastError() == cudaSuccess ? EVA_OK : EVA_ERR_CUDA;
 }
 

@@ -33,6 +33,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "decode_tc.cuh"
 #include "internal.h"
 #include "tc.cuh"
 
@@ -469,7 +470,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         // q / 8, 16-column tile q % 8); k-tile row ktl lies in 64-deep weight sub-tile ktl / 4
         const int d = warp - 2;
         const int ktl = (d * TPW) >> 3, nt0 = (d * TPW) & 7;
-        const LaneGrp lg = lane_grp<K>(lane);
+        const LaneW lw = lane_w<K>(lane);
         const uint32_t ring_s = smem_u32(ring);
         // swizzled offsets of the lane's 4 words in each of its tiles (fixed for the whole loop)
         uint32_t so[TPW][4];
@@ -483,8 +484,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             so[t][2] = sub + sw128_off(n, k + 8);
             so[t][3] = sub + sw128_off(n + 8, k + 8);
         }
-        const uint32_t tb0 = nt0 * 32 * K + lg.b0 * 4, tb1 = nt0 * 32 * K + lg.b1 * 4;
-        const uint32_t ta0 = nt0 * 32 * K + lg.a0 * 4, ta1 = nt0 * 32 * K + lg.a1 * 4;
+        const uint32_t tw0 = nt0 * 32 * K + lw.w0 * 4, tw1 = nt0 * 32 * K + lw.w1 * 4;
         const uint32_t tring = ring_s + static_cast<uint32_t>(CFG::ring_bytes) + ktl * TROW;
         for (int s = 0; s < total; ++s) {
             const int st = s % PF_STAGES, ts = s % TS;
@@ -492,16 +492,15 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             uint32_t a[TPW][4];
             if (L.dec_valid) {
                 const uint32_t tr = tring + ts * CFG::tslot;
-                uint32_t w[TPW][4];
+                uint32_t w[TPW][2];
 #pragma unroll
                 for (int t = 0; t < TPW; ++t) {
-                    w[t][0] = lds32(tr + t * 32 * K + tb0);
-                    w[t][1] = lds32(tr + t * 32 * K + tb1);
-                    w[t][2] = lds32(tr + t * 32 * K + ta0);
-                    w[t][3] = lds32(tr + t * 32 * K + ta1);
+                    w[t][0] = lds32(tr + t * 32 * K + tw0);
+                    w[t][1] = lds32(tr + t * 32 * K + tw1);
                 }
+                // two-word decode, 2 windows extracted on the FMA pipe, pairs packed by byte permutes
 #pragma unroll
-                for (int t = 0; t < TPW; ++t) decode_afrag_grp<K, true>(w[t][0], w[t][1], w[t][2], w[t][3], lg, a[t]);
+                for (int t = 0; t < TPW; ++t) decode_afrag_ww<K, 2, true>(w[t][0], w[t][1], lw, a[t]);
             }
             // the words are in registers (the decode consumed them): release the trellis slot
             __syncwarp();

@@ -287,7 +287,7 @@ class CudaEpOps:
                                           self.ws_local.numel(), out_ptr, None, self._stream())
         _lib.check(rc, "eva_moe_experts (arena)")
 
-    def experts_arena(self, own_rows: int = -1):
+    def experts_arena(self, own_rows: int = -1, mark=None):
         """Routed experts of every received row, from this rank's arena into its partial rows.
 
         With a PooledLayer (device-side expert cache), the experts the received rows select are made
@@ -335,6 +335,8 @@ class CudaEpOps:
                     res.mark_used()
                     if gi:
                         self.part.add_(tmp)
+        if mark is not None:
+            mark("experts")
         _lib.check(self.lib.eva_ep_signal_partials(ctypes.byref(P), self._stream()), "eva_ep_signal_partials")
 
     def combine_peers(self, pos, base, out_bf16, out_f32=None):
@@ -427,9 +429,21 @@ class EPMoE:
                     ops.append(dist.P2POp(dist.irecv, d[recv_offs[r]: recv_offs[r] + recv_counts[r]], gr, self.group))
         return dist.batch_isend_irecv(ops) if ops else []
 
-    def forward(self, x, *, out=None, out_f32=None, idx_out=None, w_out=None):
-        """x: BF16 [M, H] on this rank's device (M <= max_tokens); returns BF16 [M, H]."""
+    def forward(self, x, *, out=None, out_f32=None, idx_out=None, w_out=None, phases=None):
+        """x: BF16 [M, H] on this rank's device (M <= max_tokens); returns BF16 [M, H].
+
+        phases: optional list that receives (name, CUDA event) after each phase of the peer-memory
+        step, in stream order: route, dispatch (plan + pack stores into the peers' arenas), wait
+        (until every peer's rows arrived), experts, signal, combine (until every peer's partial rows
+        arrived, then the sum)."""
         cfg, ops = self.cfg, self.ops
+        mark = None
+        if phases is not None:
+            def mark(name):
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(torch.cuda.current_stream(self.device))
+                phases.append((name, ev))
+            mark("start")
         if x.dim() != 2 or x.shape[1] != cfg.hidden or x.dtype != _BF16:
             raise ValueError(f"x must be BF16 [M, {cfg.hidden}]")
         M = x.shape[0]
@@ -444,14 +458,24 @@ class EPMoE:
         if out is None:
             out = torch.empty(M, cfg.hidden, dtype=_BF16, device=self.device)
         if self.transport == "peers":
+            if mark is not None:
+                mark("route")
             fuse = ops.has_shared
             _, pos = ops.dispatch_peers(x, idx, w, all_to_self=fuse)
             base = None
             if not fuse:
                 base = ops.shared(x)
+            if mark is not None:
+                mark("dispatch")
             ops.wait_rows()
-            ops.experts_arena(own_rows=M if fuse else -1)   # own tokens' shared expert in the same launch
+            if mark is not None:
+                mark("wait")
+            ops.experts_arena(own_rows=M if fuse else -1, mark=mark)   # own tokens' shared expert in the same launch
+            if mark is not None:
+                mark("signal")
             ops.combine_peers(pos, base, out, out_f32)
+            if mark is not None:
+                mark("combine")
             return out
         seg = self.max_tokens if self.mode == "fixed" else 0
         counts, pos, sx, ssel, srw = ops.dispatch(x, idx, w, self.capacity, seg)
