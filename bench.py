@@ -62,7 +62,8 @@ def parse():
     ap.add_argument("--stack", action="store_true",
                     help="config 5: decode stream through --stack-layers MoE layers (RMSNorm + residual, "
                          "attention stubbed), expert parallel over the ranks")
-    ap.add_argument("--stack-layers", type=int, default=58)
+    ap.add_argument("--stack-layers", type=int, default=58,
+                    help="--stack: layers (0: 58, or with --residency < 1 the most the node's host memory holds)")
     ap.add_argument("--residency", type=float, default=1.0,
                     help="--stack: fraction of each rank's experts resident on the device (misses from pinned host)")
     ap.add_argument("--staging", default="device", choices=["device", "host"],
@@ -657,6 +658,22 @@ def stack_bench(args, cfg, dev, rank, world, local):
     pl = ExpertPlacement.balanced(zipf_load(cfg), world)
     mine = pl.experts_of(rank)
     cached = args.residency < 1.0
+    ram_limited = False
+    if cached:
+        # every rank pins its experts of every layer in host memory
+        rec = 3 * cfg.hidden * cfg.inter * cfg.bits // 8 + 6 * (cfg.hidden + cfg.inter)
+        per_layer = len(mine) * (rec + 4096) * int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+        fit = int(0.7 * avail // per_layer)
+        if world > 1:
+            fit = int(_max_min_over_ranks([fit], dev)[1][0])
+        if L <= 0:              # the largest layer count the host memory of the node holds
+            L, ram_limited = min(fit, 58), fit < 58
+        if L > fit or L < 1:
+            raise SystemExit(f"--residency {args.residency}: {L * per_layer / 2**30:.0f} GiB of pinned host memory over "
+                             f"the node's ranks, {avail / 2**30:.0f} GiB available; at most {fit} layers")
+    elif L <= 0:
+        L = 58
     pooled = cached and args.staging == "device"
     steps, warmup = args.steps, max(3, args.warmup)
     g = torch.Generator(device=dev)
@@ -694,13 +711,6 @@ def stack_bench(args, cfg, dev, rank, world, local):
     t_build = time.perf_counter()
     hosts, stats = [], None
     if cached:
-        # every rank pins its experts of every layer in host memory: refuse rather than exhaust it
-        rec = 3 * cfg.hidden * cfg.inter * cfg.bits // 8 + 6 * (cfg.hidden + cfg.inter)
-        need = L * len(mine) * (rec + 4096) * int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
-        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
-        if need > 0.7 * avail:
-            raise SystemExit(f"--residency {args.residency}: {need / 2**30:.0f} GiB of pinned host memory over the "
-                             f"node's ranks, {avail / 2**30:.0f} GiB available; use fewer --stack-layers")
         for li in range(L):
             lay = made(li)
             hosts.append(lay.host_copy(pinned=True))
@@ -794,6 +804,7 @@ def stack_bench(args, cfg, dev, rank, world, local):
                                    f"{world} GPUs", "layers": L, "batch": M, "global_batch": M * world,
                        "experts_per_gpu_per_layer": len(mine), "residency": args.residency,
                        "staging": args.staging if cached else None,
+                       "layers_limited_by_host_ram": ram_limited,
                        "parallelism": f"ep{world}", "exchange": EXCHANGE["peers"]},
             "residency_stats": stats,
             "wall_ms_per_step": 1e3 * wall / steps, "build_s": t_build, "device_status": st}
