@@ -171,14 +171,15 @@ __device__ __forceinline__ void had128_warp(float (&v)[4], int lane)
     v[1] = b + d;
     v[2] = a - c;
     v[3] = b - d;
-    // butterflies over the 5 lane bits
+    // butterflies over the 5 lane bits: lower lane v + o, upper lane o - v, both as one fma with the
+    // lane's sign (exactly the same roundings as the add / subtract)
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-        const bool upper = (lane & m) != 0;
+        const float sg = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
-            v[i] = upper ? (o - v[i]) : (v[i] + o);
+            v[i] = __fmaf_rn(v[i], sg, o);
         }
     }
     const float s = 0.08838834764831845f;   // 1/sqrt(128)

@@ -142,7 +142,9 @@ __device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar)
 }
 
 // NST ring stages; WAITF: decoders wait for the stage's data (false: they decode whatever the slot
-// holds, which separates shared-memory contention from copy latency); MODE: 0 one bulk copy per
+// holds, which separates shared-memory contention from copy latency; then the decoders touch no
+// barrier, the producer refills a slot only after its own previous copy into it landed, and it waits
+// for its last copies before the CTA exits, so no copy is in flight at exit); MODE: 0 one bulk copy per
 // trellis row (32 per stage), 1 one contiguous bulk copy per stage, 2 one 2-D tensor copy per stage
 // (rows row_stride apart), 3 cp.async 16-byte copies by the producer warp.
 template <int K, int NST, bool WAITF, int MODE>
@@ -169,7 +171,8 @@ __global__ void __launch_bounds__((MB_DEC + 1) * 32, 1) mb_stream(int iters, con
     if (warp == MB_DEC) {
         for (int it = 0; it < iters; ++it) {
             const int slot = it % MS_NSTAGE;
-            mbar_wait(&empty[slot], ((it / MS_NSTAGE) & 1) ^ 1, status);
+            if (WAITF) mbar_wait(&empty[slot], ((it / MS_NSTAGE) & 1) ^ 1, status);
+            else if (it >= MS_NSTAGE) mbar_wait(&full[slot], ((it / MS_NSTAGE) - 1) & 1, status);   // own copy landed
             // this CTA's stream of 32-row stages, chunk (blockIdx) of the row, rows advancing
             const size_t r0 = (static_cast<size_t>(it) * 32 + static_cast<size_t>(blockIdx.x) * 7919 * 32) % (rows_total - 32);
             const uint8_t* s0 = src + r0 * row_stride + static_cast<size_t>(blockIdx.x % 16) * row_bytes;
@@ -193,6 +196,9 @@ __global__ void __launch_bounds__((MB_DEC + 1) * 32, 1) mb_stream(int iters, con
             }
             if (lane < 8) bulk_g2s(st + 32 * 8 * 32 * 4 + lane * 1024, bsrc + lane * 1024, 1024, &full[slot]);
         }
+        if (!WAITF)   // the last copy of every slot has landed before the CTA may exit
+            for (int it = iters > MS_NSTAGE ? iters - MS_NSTAGE : 0; it < iters; ++it)
+                mbar_wait(&full[it % MS_NSTAGE], (it / MS_NSTAGE) & 1, status);
     } else {
         const int quad = warp >> 1, whalf = warp & 1;
         const LaneW dw = lane_w<K>(lane);
@@ -219,7 +225,7 @@ __global__ void __launch_bounds__((MB_DEC + 1) * 32, 1) mb_stream(int iters, con
                 }
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (WAITF && lane == 0) mbar_arrive(&empty[slot]);
         }
         float sm = 0.0f;
 #pragma unroll

@@ -322,11 +322,11 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
         // index bits 3-4: r (lane bits 0-1)
 #pragma unroll
         for (int m = 1; m < 4; m <<= 1) {
-            const bool upper = (r & m) != 0;
+            const float sg = (r & m) ? -1.0f : 1.0f;   // upper lane o - v, lower v + o, as one fma
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
                 const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
-                v[i] = upper ? (o - v[i]) : (v[i] + o);
+                v[i] = __fmaf_rn(v[i], sg, o);
             }
         }
         // index bits 5-6: j
