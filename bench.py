@@ -198,13 +198,19 @@ def prefill_measure(cfg, layer, dev, steps, warmup, M):
     flop_router = 2.0 * M * cfg.hidden * cfg.n_experts
     peak, kind = tensor_peak()
     share = np.sort(loads)[::-1] / loads.sum()
-    # 256-row expert tiles the CTA pairs run (each decodes its expert's weights once): routed + shared
-    tiles = int(np.sum((loads + 255) // 256)) + ((M + 255) // 256 if cfg.shared_inter else 0)
+    # 256-row expert tiles the CTA pairs run (each decodes its expert's weights once): routed + shared;
+    # a tile of at most 128 rows runs at half height (M = 128 pair MMAs)
+    counts = [int(n) for n in loads if n > 0] + ([M] if cfg.shared_inter else [])
+    tiles = sum((n + 255) // 256 for n in counts)
+    half = sum(1 for n in counts if 0 < n % 256 <= 128)
+    mma_rows = 256 * tiles - 128 * half
     return {"metric": "moe_layer_prefill_tokens_per_s", "value": M / (ms * 1e-3), "unit": "tokens/s",
             "tokens_per_step": M, "ms_per_step": ms, "steps": steps,
             "routing": f"router bias + {ZIPF_BETA} * log(rank^-{ZIPF_S}) (Zipf-skewed); expert load top-8 share "
                        f"{share[:8].sum():.3f}, top-32 {share[:32].sum():.3f}, experts used {(loads > 0).sum()}",
-            "expert_tiles": {"tiles_256_rows": tiles, "row_fill": (M * cfg.topk + (M if cfg.shared_inter else 0)) / (tiles * 256.0),
+            "expert_tiles": {"tiles": tiles, "half_height_tiles": half,
+                             "row_fill": (M * cfg.topk + (M if cfg.shared_inter else 0)) / mma_rows,
+                             "row_fill_if_all_256": (M * cfg.topk + (M if cfg.shared_inter else 0)) / (tiles * 256.0),
                              "experts_used": int((loads > 0).sum()) + (1 if cfg.shared_inter else 0)},
             "roofline": {"bound": "tensor", "achieved": (flop_exp) / (ems * 1e-3) / 1e12, "peak": peak, "unit": "TFLOP/s",
                          "frac": (flop_exp) / (ems * 1e-3) / 1e12 / peak, "peak_kind": kind,

@@ -541,8 +541,9 @@ extern "C" int eva_decode_microbench(int32_t variant, int32_t bits, int32_t iter
 extern "C" int eva_tc_selftest(int32_t what, const uint32_t* a, const uint32_t* b, uint32_t* out, int32_t* status,
                                void* stream)
 {
-    if (what < 0 || what > 2 || !out || !status || (what > 0 && (!a || !b))) return EVA_ERR_INVALID;
+    if (what < 0 || what > 4 || !out || !status || ((what == 1 || what == 2) && (!a || !b))) return EVA_ERR_INVALID;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (what >= 3) return pf_pair_selftest_launch(what == 3 ? 256 : 128, out, status, st) == cudaSuccess ? EVA_OK : EVA_ERR_CUDA;
     tc_selftest<<<1, 128, 0, st>>>(what, a, b, out, status);
     return cudaGetLastError() == cudaSuccess ? EVA_OK : EVA_ERR_CUDA;
 }

@@ -122,4 +122,7 @@ cudaError_t launch_dequant(const void* trellis, int in, int out, int K, uint16_t
 
 int num_sms();
 
+// Pair-MMA layout self-test (prefill.cu), M = 256 or 128: out[2][128][256] u32.
+cudaError_t pf_pair_selftest_launch(int M, uint32_t* out, int* status, cudaStream_t stream);
+
 }  // namespace eva

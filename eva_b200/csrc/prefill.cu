@@ -7,10 +7,13 @@
 // the tensor cores of both SMs read both halves, and each CTA's TMEM receives its 128 rows x 256
 // columns. Per SM this reads half the shared-memory bytes per MAC of a one-SM 128 x 128 tile,
 // which is what bounds a tcgen05 kernel whose weights are written to shared memory by warps.
+// A tile of at most 128 rows (an expert's last, or a small expert's only tile) runs as M = 128
+// pair MMAs instead: each CTA holds 64 rows, the tensor work on padding rows halves, the decode is
+// unchanged (its accumulators lie folded in TMEM: pf_tmem_to_smem_half).
 //   warp 0      activation producer: 2-D TMA loads of the CTA's activation rows (completion counted
 //               on the leader CTA's barrier) into the activation/weight ring (PfCfg: stages, depth)
-//   last warp   trellis producer: 1-D bulk copies of the CTA's trellis rows into a ring of their
-//               own, whose slots the decoders release as soon as they have read their words
+//   last warp   trellis producer: one 2-D tensor copy per stage (per-expert maps from pf_maps) of
+//               the CTA's trellis rows into a ring of their own, whose slots the decoders release as soon as they have read their words
 //   warps 2..   decoders: EXL3 decode of the stage's weight tiles into raw codebook values
 //               h = 1024 + bytesum (exact fp16) straight into the UMMA K-major 128B-swizzled layout;
 //               they arrive on the leader's barrier (the peer CTA's from across the cluster). The
@@ -170,11 +173,103 @@ __device__ __forceinline__ void sts32(uint32_t addr, uint32_t v)
     asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ uint8_t* pf_ring_align(uint8_t* raw)
+{
+    const uint32_t a = smem_u32(raw);
+    return raw + ((1024 - (a & 1023)) & 1023);
+}
+
 // Byte offset of element (row, k) (k < 64, fp16) in a K-major 128B-swizzled 128 x 64 tile.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k)
 {
     const int kb = k * 2;
     return row * 128 + ((((kb >> 4) ^ (row & 7)) << 4) | (kb & 15));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Layout self-test of the pair MMA (eva_tc_selftest what 3 / 4): one cluster of two CTAs, one
+// tcgen05.mma.cta_group::2.kind::f16 of M = 256 or 128 rows (CTA r holds rows M/2 r .. M/2 r + M/2 - 1
+// of A), N = 256 (CTA r holds B rows 128 r .. 128 r + 127), K = 16, with A[i][0] = i + 1,
+// A[i][1] = 256, B[n][0] = 1, B[n][1] = n + 1 and zeros elsewhere, so D[i][n] = (i + 1) + 256 (n + 1)
+// names its own row and column. Each CTA fills its 256 TMEM columns with 0xffffffff first, then
+// writes every lane and column it holds after the MMA: out[rank][lane 0..127][col 0..255].
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(128)
+    pf_pair_selftest(int M, uint32_t* out, int* status)
+{
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t accb;
+    __shared__ uint32_t tmem_slot;
+    uint8_t* sm = pf_ring_align(smem_raw);
+    const uint32_t rank = cluster_ctarank();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* A = sm;
+    uint8_t* B = sm + PF_A_BYTES;
+    for (int i = threadIdx.x; i < (PF_A_BYTES + PF_B_BYTES) / 4; i += blockDim.x) reinterpret_cast<uint32_t*>(sm)[i] = 0;
+    __syncthreads();
+    {
+        const int i = threadIdx.x;   // local row of A and of B
+        const int grow = static_cast<int>(rank) * (M / 2) + i;
+        if (i < M / 2) {
+            *reinterpret_cast<__half*>(A + sw128_off(i, 0)) = __float2half(static_cast<float>(grow + 1));
+            *reinterpret_cast<__half*>(A + sw128_off(i, 1)) = __float2half(256.0f);
+        }
+        const int n = static_cast<int>(rank) * 128 + i;
+        *reinterpret_cast<__half*>(B + sw128_off(i, 0)) = __float2half(1.0f);
+        *reinterpret_cast<__half*>(B + sw128_off(i, 1)) = __float2half(static_cast<float>(n + 1));
+    }
+    fence_proxy_async_smem();
+    if (threadIdx.x == 0) {
+        mbar_init(&accb, 1);
+        fence_barrier_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)), "r"(256));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    {
+        uint32_t r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = 0xffffffffu;
+        for (int c = 0; c < 256; c += 8) tmem_st32x32_x8(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, r);
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    tc_fence_after();
+    if (rank == 0 && threadIdx.x == 0) {
+        umma_f16_pair(tmem, umma_desc_sw128(smem_u32(A)), umma_desc_sw128(smem_u32(B)),
+                      M == 128 ? umma_idesc_f16(128, 256) : umma_idesc_f16(256, 256), 0u);
+        umma_commit_pair(mapa_rank(&accb, 0));
+        umma_commit_pair(mapa_rank(&accb, 1));
+    }
+    mbar_wait(&accb, 0, status);
+    tc_fence_after();
+    for (int c = 0; c < 256; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + c, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            out[(static_cast<size_t>(rank) * 128 + warp * 32 + lane) * 256 + c + j] = __float_as_uint(v[j]);
+    }
+    tc_fence_before();
+    cluster_sync_all();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256));
+    }
+}
+
+cudaError_t pf_pair_selftest_launch(int M, uint32_t* out, int* status, cudaStream_t stream)
+{
+    const int smem = 1024 + PF_A_BYTES + PF_B_BYTES;
+    cudaError_t e = cudaFuncSetAttribute(pf_pair_selftest, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    pf_pair_selftest<<<2, 128, smem, stream>>>(M, out, status);
+    return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -376,6 +471,7 @@ struct PfLoop {
     int chunk, dec_valid;
     int nproj, nkb, row0;    // row0: this CTA's first activation row
     uint32_t rank;           // 0 = leader (issues the MMAs)
+    int half;                // tile of <= 128 rows: M = 128 pair MMAs, 64 rows per CTA
 };
 
 template <int NS>
@@ -438,7 +534,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         if (L.rank != 0 || lane != 0) return;
         // leader, one thread: pair MMAs (M = 256 over both CTAs' rows, N = 256 over both CTAs'
         // decoded columns), one commit per stage
-        constexpr uint32_t idesc = umma_idesc_f16(2 * PF_BM, PF_PAIR_N);
+        const uint32_t idesc = L.half ? umma_idesc_f16(PF_BM, PF_PAIR_N) : umma_idesc_f16(2 * PF_BM, PF_PAIR_N);
         int st = 0, pj = 0, kb = 0;
         uint32_t ph = 0;
         for (int s = 0; s < total; ++s) {
@@ -534,6 +630,22 @@ __device__ __forceinline__ void pf_tmem_to_smem(uint32_t tmem, int col0, float* 
         tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + col0 + c * 32, v);
 #pragma unroll
         for (int i = 0; i < 32; ++i) tile[row * PF_EPI_LD + c * 32 + i] = v[i];
+    }
+}
+
+// Half-height tiles (M = 128 pair MMAs): a CTA's 64 rows x 256 columns lie folded in its TMEM, lane
+// l < 64 holding row l, columns 0..127 and lane 64 + l row l, columns 128..255 (from col0). Chunk c
+// (the pair's columns 128 c .. 128 c + 127) -> smem tile [64][PF_EPI_LD] by warps 2 c and 2 c + 1.
+__device__ __forceinline__ void pf_tmem_to_smem_half(uint32_t tmem, int col0, int c, float* tile, int warp, int lane)
+{
+    if ((warp >> 1) != c) return;
+    const int row = (warp & 1) * 32 + lane;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+        float v[32];
+        tmem_ld32(tmem + (static_cast<uint32_t>(warp * 32) << 16) + col0 + cc * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) tile[row * PF_EPI_LD + cc * 32 + i] = v[i];
     }
 }
 
@@ -641,7 +753,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
     L.dec_valid = L.chunk < nch;
     L.nproj = 2;
     L.nkb = p.H / (PF_BK * CFG::ksub);                     // H is a multiple of 128
-    L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
+    L.half = t.rows <= PF_BM;
+    const int cta_rows = L.half ? PF_BM / 2 : PF_BM;
+    L.row0 = t.row0 + static_cast<int>(rank) * cta_rows;
     L.rank = rank;
     if (Ke == KR) pf_mainloop<KR, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
     else pf_mainloop<KS, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
@@ -651,7 +765,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
     tc_fence_after();
     float* G = reinterpret_cast<float*>(ring);
     float* U = G + PF_BM * PF_EPI_LD;
-    const int rows = min(PF_BM, t.rows - static_cast<int>(rank) * PF_BM);
+    const int rows = min(cta_rows, t.rows - static_cast<int>(rank) * cta_rows);
     const int mode = t.shared ? p.act_shared : p.act_routed;
     // raw codebook: x . w = c0 (x . h) + c1 sum(x), sum(x) over the row's stored fp16 inputs
     __shared__ float rsum[2][PF_BM];
@@ -666,8 +780,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
         const int chunk = 2 * pc + c;
         if (chunk >= nch) break;
         if (warp < 4) {
-            pf_tmem_to_smem(S.tmem, c * PF_BN, G, warp, lane);
-            pf_tmem_to_smem(S.tmem, PF_PAIR_N + c * PF_BN, U, warp, lane);
+            if (L.half) {
+                pf_tmem_to_smem_half(S.tmem, 0, c, G, warp, lane);
+                pf_tmem_to_smem_half(S.tmem, PF_PAIR_N, c, U, warp, lane);
+            } else {
+                pf_tmem_to_smem(S.tmem, c * PF_BN, G, warp, lane);
+                pf_tmem_to_smem(S.tmem, PF_PAIR_N + c * PF_BN, U, warp, lane);
+            }
         }
         __syncthreads();
         const int col = chunk * 128 + lane * 4;
@@ -731,7 +850,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
     L.dec_valid = 1;                                       // H is a multiple of 256
     L.nproj = 1;
     L.nkb = I_e / (PF_BK * CFG::ksub);
-    L.row0 = t.row0 + static_cast<int>(rank) * PF_BM;
+    L.half = t.rows <= PF_BM;
+    const int cta_rows = L.half ? PF_BM / 2 : PF_BM;
+    L.row0 = t.row0 + static_cast<int>(rank) * cta_rows;
     L.rank = rank;
     if (Ke == KR) pf_mainloop<KR, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
     else pf_mainloop<KS, CFG>(L, ring, S.bars, S.tmem, warp, lane, p.status);
@@ -739,12 +860,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
     mbar_wait(&S.bars.accb, 0, p.status);
     tc_fence_after();
     float* D = reinterpret_cast<float*>(ring);
-    const int rows = min(PF_BM, t.rows - static_cast<int>(rank) * PF_BM);
+    const int rows = min(cta_rows, t.rows - static_cast<int>(rank) * cta_rows);
     // raw codebook correction with the sums of the rows' stored fp16 down inputs
     __shared__ float rsum[PF_BM];
     if (threadIdx.x < PF_BM * 2) pf_row_sums<2>(p.asum, p.imax / 128, I_e / 128, L.row0, rows, rsum, PF_BM * 2);
     for (int c = 0; c < 2; ++c) {
-        if (warp < 4) pf_tmem_to_smem(S.tmem, c * PF_BN, D, warp, lane);
+        if (warp < 4) {
+            if (L.half) pf_tmem_to_smem_half(S.tmem, 0, c, D, warp, lane);
+            else pf_tmem_to_smem(S.tmem, c * PF_BN, D, warp, lane);
+        }
         __syncthreads();
         const int col = (2 * pc + c) * 128 + lane * 4;
         float svd[4];

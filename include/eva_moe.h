@@ -362,7 +362,10 @@ int eva_host_mapped(const void* p);
  * (32x32b) after 16x256b.x2 stores of tags (half << 12 | lane << 4 | register) at lanes 32 w + 16 half;
  * what 1: out[128][16] s32 = A x B^T with A u8 [128][32] stored in TMEM, B s8 [16][32] in shared
  * memory (tcgen05.mma.kind::i8); what 2: out[128][16] f32 = A x B^T with A f16 [128][16] in TMEM and
- * B f16 [16][16] (kind::f16). a, b: device arrays of those shapes (what > 0); status: device int32. */
+ * B f16 [16][16] (kind::f16); what 3 / 4: a cluster of two CTAs runs one tcgen05.mma.cta_group::2.kind::f16
+ * of M = 256 / 128 rows and N = 256 whose D[i][n] = (i + 1) + 256 (n + 1), each CTA dumps its 128 TMEM
+ * lanes x 256 columns (0xffffffff where the MMA wrote nothing): out[2][128][256] u32. a, b: device
+ * arrays of those shapes (what 1, 2); status: device int32. */
 int eva_decode_microbench(int32_t variant, int32_t bits, int32_t iters, double* out, void* stream);
 int eva_tc_selftest(int32_t what, const uint32_t* a, const uint32_t* b, uint32_t* out, int32_t* status, void* stream);
 

@@ -6,6 +6,8 @@
   columns k of the weight tile without any exchange between lanes (eva_b200/csrc/decode_tc.cuh).
 * tcgen05.mma.kind::i8 (u8 x s8 -> s32) and kind::f16 with the A operand read from TMEM and B from
   128B-swizzled shared memory compute A x B^T (M 128, N 16).
+* The pair MMA (tcgen05.mma.cta_group::2) places its accumulators as the prefill kernels read them,
+  for full (M = 256) and half-height (M = 128) tiles.
 * The decode micro-benchmark runs every variant to completion with a clean device status.
 """
 import ctypes
@@ -20,16 +22,16 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-def _selftest(what, a=None, b=None):
+def _selftest(what, a=None, b=None, shape=(128, 16)):
     lib = _lib.load()
-    out = torch.zeros(128 * 16, dtype=torch.int32, device=DEV)
+    out = torch.zeros(int(np.prod(shape)), dtype=torch.int32, device=DEV)
     st = torch.zeros(1, dtype=torch.int32, device=DEV)
     rc = lib.eva_tc_selftest(what, None if a is None else a.data_ptr(), None if b is None else b.data_ptr(),
                              out.data_ptr(), st.data_ptr(), torch.cuda.current_stream().cuda_stream)
     _lib.check(rc, "eva_tc_selftest")
     torch.cuda.synchronize()
     assert int(st.item()) == 0
-    return out.cpu().numpy().view(np.uint32).reshape(128, 16)
+    return out.cpu().numpy().view(np.uint32).reshape(shape)
 
 
 def test_tmem_16x256b_store_layout():
@@ -75,3 +77,22 @@ def test_decode_microbench_runs(variant):
     _lib.check(lib.eva_decode_microbench(variant, 3, 64, out, torch.cuda.current_stream().cuda_stream),
                "eva_decode_microbench")
     assert out[3] == 0 and out[0] > 0
+
+
+@pytest.mark.parametrize("M", [256, 128])
+def test_pair_mma_tmem_layout(M):
+    """tcgen05.mma.cta_group::2 (kind::f16, N = 256): with M = 256, CTA r's TMEM lane l, column c holds
+    D[128 r + l][c]; with M = 128 each CTA's 64 rows x 256 columns are folded into 128 lanes x 128
+    columns: lane l < 64 holds row 64 r + l, columns 0..127, lane l >= 64 row 64 r + l - 64, columns
+    128..255 (the prefill kernels' half-height tiles read their accumulators this way)."""
+    out = _selftest(3 if M == 256 else 4, shape=(2, 128, 256))
+    want = np.full((2, 128, 256), 0xffffffff, np.uint32)
+    for r in range(2):
+        for lane in range(128):
+            if M == 256:
+                i, cols, n0 = 128 * r + lane, 256, 0
+            else:
+                i, cols, n0 = 64 * r + lane % 64, 128, 128 * (lane // 64)
+            n = np.arange(cols) + n0
+            want[r, lane, :cols] = np.float32((i + 1) + 256 * (n + 1)).view(np.uint32)
+    assert np.array_equal(out, want)
