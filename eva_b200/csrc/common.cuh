@@ -187,6 +187,26 @@ __device__ __forceinline__ void had128_warp(float (&v)[4], int lane)
     for (int i = 0; i < 4; ++i) v[i] *= s;
 }
 
+// Explicit shared-space accesses for decoding warps (generic accesses wait on the long scoreboard).
+__device__ __forceinline__ uint32_t lds32(uint32_t addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v)
+{
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // Half/bf16 helpers
 
@@ -422,7 +442,10 @@ __device__ __forceinline__ float act_gated(float g, float u, float limit, int mo
         }
         return g / (1.0f + expf(-g)) * u;
     }
-    float a = g / (1.0f + expf(-g));
+    // the routed experts' SiLU with the fast exponential and reciprocal, as the reference's coop
+    // kernels evaluate it (exl3_moe_coop_kernel.cuh:80-84): a few ulp from the correctly rounded value,
+    // an eighth of the instructions of expf and an IEEE division
+    float a = g * __fdividef(1.0f, 1.0f + __expf(-g));
     if (limit != 0.0f) {
         u = fminf(fmaxf(u, -limit), limit);
         a = fminf(a, limit);

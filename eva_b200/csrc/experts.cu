@@ -236,21 +236,30 @@ constexpr int WR = 4;   // k-tile rows per warp per stage
 // shared-memory read from the stage's copy of the lane's token row (fragment layout).
 __device__ __forceinline__ void load_b4_smem(const uint8_t* brow, int g, int lane, uint32_t (&b)[2 * WR])
 {
-    const uint4* p = reinterpret_cast<const uint4*>(brow + g * 128 + (lane & 3) * 32);
-    const uint4 u0 = p[0], u1 = p[1];
+    const uint32_t a = smem_u32(brow + g * 128 + (lane & 3) * 32);
+    const uint4 u0 = lds128(a), u1 = lds128(a + 16);
     b[0] = u0.x; b[1] = u0.y; b[2] = u0.z; b[3] = u0.w;
     b[4] = u1.x; b[5] = u1.y; b[6] = u1.z; b[7] = u1.w;
 }
 
 
+// One k-tile row of a warp's stage: its WT tiles' words (explicit shared-memory loads, all issued
+// before the first decode), then decode + MMA per tile. tiles: shared-memory address of the row's
+// first tile.
 template <int K>
-__device__ __forceinline__ void gemv_row_w(const uint32_t* tiles, const LaneW& d, uint32_t b0, uint32_t b1,
+__device__ __forceinline__ void gemv_row_w(uint32_t tiles, const LaneW& d, uint32_t b0, uint32_t b1,
                                            float (&acc)[WT][4])
 {
+    uint32_t w[WT][2];
+#pragma unroll
+    for (int t = 0; t < WT; ++t) {
+        w[t][0] = lds32(tiles + (t * 8 * K + d.w0) * 4);
+        w[t][1] = lds32(tiles + (t * 8 * K + d.w1) * 4);
+    }
 #pragma unroll
     for (int t = 0; t < WT; ++t) {
         uint32_t a[4];
-        decode_afrag_w<K, 2, true>(tiles + t * 8 * K, d, a);
+        decode_afrag_ww<K, 2, true>(w[t][0], w[t][1], d, a);
         mma_16816(acc[t], a, b0, b1);
     }
 }
@@ -261,14 +270,14 @@ template <int K>
 __device__ __forceinline__ void gemv_stage(const uint32_t* buf, const LaneW& d, int quad, int whalf, int r0, int ke,
                                            const uint32_t (&b)[2 * WR], float (&acc)[WT][4])
 {
-    const uint32_t* rowp = buf + ((WR * quad) * NT + WT * whalf) * 8 * K;
+    const uint32_t rowp = smem_u32(buf + ((WR * quad) * NT + WT * whalf) * 8 * K);
     if (r0 + WR <= ke) {
 #pragma unroll
-        for (int r = 0; r < WR; ++r) gemv_row_w<K>(rowp + r * NT * 8 * K, d, b[2 * r], b[2 * r + 1], acc);
+        for (int r = 0; r < WR; ++r) gemv_row_w<K>(rowp + r * NT * 8 * K * 4, d, b[2 * r], b[2 * r + 1], acc);
     } else {
 #pragma unroll
         for (int r = 0; r < WR; ++r)
-            if (r0 + r < ke) gemv_row_w<K>(rowp + r * NT * 8 * K, d, b[2 * r], b[2 * r + 1], acc);
+            if (r0 + r < ke) gemv_row_w<K>(rowp + r * NT * 8 * K * 4, d, b[2 * r], b[2 * r + 1], acc);
     }
 }
 
