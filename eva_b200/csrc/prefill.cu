@@ -621,6 +621,23 @@ __device__ __forceinline__ void pf_tmem_to_smem(uint32_t tmem, int col0, float* 
     }
 }
 
+// Epilogue rows in the lane-strided order: lane l holds elements l, l + 32, l + 64, l + 96 of a
+// 128-column chunk, so that a warp's reads of a 129-float tile row hit 32 different banks (a lane
+// holding 4 consecutive elements would share banks four ways). had128_warp is applied to this order
+// unchanged: the Sylvester transform commutes with any permutation of the index bits applied to input
+// and output alike, and here the register index is bits 5-6 and the lane bits 0-4.
+__device__ __forceinline__ void load4s_half(const __half* p, int lane, float (&v)[4])
+{
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __half2float(__ldg(p + lane + 32 * i));
+}
+
+__device__ __forceinline__ void store4s_half(__half* p, int lane, const float (&v)[4])
+{
+#pragma unroll
+    for (int i = 0; i < 4; ++i) p[lane + 32 * i] = __float2half_rn(v[i]);
+}
+
 // Half-height tiles (M = 128 pair MMAs): a CTA's 64 rows x 256 columns lie folded in its TMEM, lane
 // l < 64 holding row l, columns 0..127 and lane 64 + l row l, columns 128..255 (from col0). Chunk c
 // (the pair's columns 128 c .. 128 c + 127) -> smem tile [64][PF_EPI_LD] by warps 2 c and 2 c + 1.
@@ -777,26 +794,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
             }
         }
         __syncthreads();
-        const int col = chunk * 128 + lane * 4;
+        const int col = chunk * 128;   // lane-strided rows (load4s_half)
         float svg[4], svu[4], sud[4];
-        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 2)) + col, svg);
-        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 5)) + col, svu);
-        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 7)) + col, sud);
+        load4s_half(reinterpret_cast<const __half*>(pf_ptr(p, t, 2)) + col, lane, svg);
+        load4s_half(reinterpret_cast<const __half*>(pf_ptr(p, t, 5)) + col, lane, svu);
+        load4s_half(reinterpret_cast<const __half*>(pf_ptr(p, t, 7)) + col, lane, sud);
         for (int r = warp; r < rows; r += PF_THREADS / 32) {
             const int pos = L.row0 + r;
             const float sg = rsum[0][r], su = rsum[1][r];
             float g[4], u[4], a[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                g[i] = CB_C0 * G[r * PF_EPI_LD + lane * 4 + i] + CB_C1 * sg;
-                u[i] = CB_C0 * U[r * PF_EPI_LD + lane * 4 + i] + CB_C1 * su;
+                g[i] = CB_C0 * G[r * PF_EPI_LD + lane + 32 * i] + CB_C1 * sg;
+                u[i] = CB_C0 * U[r * PF_EPI_LD + lane + 32 * i] + CB_C1 * su;
             }
             had128_warp(g, lane);
             had128_warp(u, lane);
 #pragma unroll
             for (int i = 0; i < 4; ++i) a[i] = act_gated(g[i] * svg[i], u[i] * svu[i], p.limit, mode) * sud[i];
             had128_warp(a, lane);
-            store4_half(p.ap + static_cast<size_t>(pos) * p.imax + col, a);
+            store4s_half(p.ap + static_cast<size_t>(pos) * p.imax + col, lane, a);
             float sa = 0.0f;   // sum of the values as stored (fp16), for the down projection's correction
 #pragma unroll
             for (int i = 0; i < 4; ++i) sa += __half2float(__float2half_rn(a[i]));
@@ -858,20 +875,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfDownCfg::threads, 
             else pf_tmem_to_smem(S.tmem, c * PF_BN, D, warp, lane);
         }
         __syncthreads();
-        const int col = (2 * pc + c) * 128 + lane * 4;
+        const int col = (2 * pc + c) * 128;   // lane-strided rows (load4s_half)
         float svd[4];
-        load4_half_ro(reinterpret_cast<const __half*>(pf_ptr(p, t, 8)) + col, svd);
+        load4s_half(reinterpret_cast<const __half*>(pf_ptr(p, t, 8)) + col, lane, svd);
         for (int r = warp; r < rows; r += PF_THREADS / 32) {
             const int slot = pf_row_slot(p, L.row0 + r);
             const float w = t.shared ? 1.0f : p.rw[slot];
             const float sa = rsum[r];
             float v[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) v[i] = CB_C0 * D[r * PF_EPI_LD + lane * 4 + i] + CB_C1 * sa;
+            for (int i = 0; i < 4; ++i) v[i] = CB_C0 * D[r * PF_EPI_LD + lane + 32 * i] + CB_C1 * sa;
             had128_warp(v, lane);
 #pragma unroll
             for (int i = 0; i < 4; ++i) v[i] *= svd[i] * w;
-            *reinterpret_cast<float4*>(p.dpart + static_cast<size_t>(slot) * p.H + col) = make_float4(v[0], v[1], v[2], v[3]);
+            float* dst = p.dpart + static_cast<size_t>(slot) * p.H + col;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = v[i];
         }
         __syncthreads();
     }
