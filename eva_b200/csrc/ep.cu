@@ -361,12 +361,19 @@ __global__ void __launch_bounds__(PACK_THREADS) ep_pack_peers_kernel(EpDispatchA
 }
 
 // One warp: lane r waits until flag(r) >= this rank's epoch (bounded).
-template <bool ROWS>
+// PUBLISH (the partials wait): thread 0 first publishes this rank's partial sums, as ep_signal_kernel
+// does (the experts launch that wrote them has completed before this launch), so that a step needs no
+// launch of its own for the signal.
+template <bool ROWS, bool PUBLISH = false>
 __global__ void __launch_bounds__(32) ep_wait_kernel(EvaEpPeers P, int32_t* status)
 {
     const int r = threadIdx.x;
-    if (r >= P.world) return;
     const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(flag_at(P, P.rank, FLAG_EPOCH));
+    if (PUBLISH && r == 0) {
+        __threadfence_system();
+        st_release_sys(flag_at(P, P.rank, FLAG_PART), ep);
+    }
+    if (r >= P.world) return;
     const uint32_t* f = ROWS ? flag_at(P, P.rank, FLAG_ROWS + 4 * r) : flag_at(P, r, FLAG_PART);
     if (ld_acquire_sys(f) >= ep) return;
     const uint64_t t0 = globaltimer();
@@ -530,7 +537,7 @@ extern "C" int eva_ep_combine_peers(const EvaEpPeers* p, int32_t M, const int32_
     if (!peers_ok(p) || M < 0 || (!out_f32 && !out_bf16) || (M > 0 && !pos)) return EVA_ERR_INVALID;
     if (!al16(base) || !al16(out_f32) || (reinterpret_cast<uintptr_t>(out_bf16) & 7)) return EVA_ERR_INVALID;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    ep_wait_kernel<false><<<1, 32, 0, s>>>(*p, status);
+    ep_wait_kernel<false, true><<<1, 32, 0, s>>>(*p, status);
     if (M > 0) {
         const long long n = static_cast<long long>(M) * (p->H / 4);
         const long long blocks = (n + 255) / 256;

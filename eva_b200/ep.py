@@ -337,7 +337,7 @@ class CudaEpOps:
                         self.part.add_(tmp)
         if mark is not None:
             mark("experts")
-        _lib.check(self.lib.eva_ep_signal_partials(ctypes.byref(P), self._stream()), "eva_ep_signal_partials")
+        # the partials are published by the combine launch (eva_ep_combine_peers), first thing
 
     def combine_peers(self, pos, base, out_bf16, out_f32=None):
         rc = self.lib.eva_ep_combine_peers(ctypes.byref(self.peers), pos.shape[1], pos.data_ptr(), _lib.ptr(base),
@@ -434,8 +434,8 @@ class EPMoE:
 
         phases: optional list that receives (name, CUDA event) after each phase of the peer-memory
         step, in stream order: route, dispatch (plan + pack stores into the peers' arenas), wait
-        (until every peer's rows arrived), experts, signal, combine (until every peer's partial rows
-        arrived, then the sum)."""
+        (until every peer's rows arrived), experts, combine (publish this rank's partials, wait until
+        every peer's arrived, then the sum)."""
         cfg, ops = self.cfg, self.ops
         mark = None
         if phases is not None:
@@ -471,9 +471,7 @@ class EPMoE:
             if mark is not None:
                 mark("wait")
             ops.experts_arena(own_rows=M if fuse else -1, mark=mark)   # own tokens' shared expert in the same launch
-            if mark is not None:
-                mark("signal")
-            ops.combine_peers(pos, base, out, out_f32)
+            ops.combine_peers(pos, base, out, out_f32)   # publishes this rank's partials, then waits for all
             if mark is not None:
                 mark("combine")
             return out

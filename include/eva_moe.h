@@ -228,9 +228,9 @@ int eva_ep_combine(int32_t H, int32_t M, int32_t world, const float* back, const
  *   part      float [world][segment_rows][H]: this rank's routed partial sums of the received rows
  * A step: eva_ep_dispatch_peers (plan; each row stored straight into its destination's recv_*; the
  * last block releases every destination's "rows ready" flag for this source) -> eva_ep_wait_rows
- * -> eva_moe_experts on the recv_* rows into part -> eva_ep_signal_partials -> eva_ep_combine_peers
- * (waits for every rank's "partials ready" flag, then reads the partial rows of this rank's tokens
- * from the peers' arenas). Flags hold step numbers, so no reset is needed between steps, and a
+ * -> eva_moe_experts on the recv_* rows into part -> eva_ep_combine_peers (publishes this rank's
+ * "partials ready" flag, waits for every rank's, then reads the partial rows of this rank's tokens
+ * from the peers' arenas; eva_ep_signal_partials publishes the flag earlier, on its own). Flags hold step numbers, so no reset is needed between steps, and a
  * rank cannot overwrite a peer's rows before the peer has finished the previous step (its combine
  * waited for that peer's partials). Every wait is bounded (2 s) and sets EVA_STATUS_TIMEOUT. */
 #define EVA_EP_MAX_WORLD 32
@@ -266,10 +266,12 @@ int eva_ep_dispatch_peers(const EvaEpPeers* p, const void* x, int32_t M, const i
                           int32_t all_to_self, int32_t* counts, int32_t* pos, int32_t* status, void* stream);
 /* Wait until every source's rows of this step are in this rank's arena. */
 int eva_ep_wait_rows(const EvaEpPeers* p, int32_t* status, void* stream);
-/* Publish this rank's partial sums of this step (after the experts launch that wrote part). */
+/* Publish this rank's partial sums of this step (after the experts launch that wrote part); optional,
+ * eva_ep_combine_peers publishes them too. */
 int eva_ep_signal_partials(const EvaEpPeers* p, void* stream);
-/* out[m] = base[m] + sum over r (rank order) of rank r's partial row for token m; waits for every
- * rank's partials first. base: float [M][H] or NULL; out_f32 / out_bf16 at least one. */
+/* out[m] = base[m] + sum over r (rank order) of rank r's partial row for token m; publishes this
+ * rank's partials (stream order after the experts launch that wrote part) and waits for every rank's
+ * first. base: float [M][H] or NULL; out_f32 / out_bf16 at least one. */
 int eva_ep_combine_peers(const EvaEpPeers* p, int32_t M, const int32_t* pos, const float* base, float* out_f32,
                          void* out_bf16, int32_t* status, void* stream);
 

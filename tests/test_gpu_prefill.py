@@ -109,3 +109,37 @@ def test_forward_dispatches_prefill_for_large_batches(oracle):
     assert np.array_equal(idx.cpu().numpy(), ridx)
     ref = oracle.moe_forward(x.view(torch.int16).numpy().view(np.uint16), ridx, rwt, layer)
     close(out.cpu().numpy(), ref, 3e-3, 0.99999)
+
+
+def routes_with_counts(counts, M, topk, rng):
+    """Routes in which expert e is selected by exactly counts[e] of the M rows (topk distinct experts
+    per row): each row takes the topk experts with the most selections left."""
+    left = np.array(counts, dtype=np.int64)
+    assert left.sum() == M * topk and left.max() <= M
+    sel = np.empty((M, topk), dtype=np.int64)
+    for m in range(M):
+        pick = np.argsort(-left, kind="stable")[:topk]
+        assert (left[pick] > 0).all()
+        left[pick] -= 1
+        sel[m] = rng.permutation(pick)
+    return sel[rng.permutation(M)]
+
+
+def test_prefill_tile_heights_vs_oracle(oracle):
+    """Experts whose row counts straddle the tile boundaries: 1, 63, 64, 65, 127, 128 rows (one
+    half-height tile; the second CTA of the pair holds no rows, one row, or up to 64), 129, 255 (one
+    full tile), 257 (a full tile and a half-height tail), and the shared expert's 320 rows (a full
+    tile and a 64-row tail), against the FP64 oracle."""
+    lib = _lib.load()
+    cfg = SMALL
+    M = 320
+    counts = [1, 63, 64, 65, 127, 128, 129, 255, 257, 0, 2, 30, 31, 33, 95, 0]
+    rng = np.random.default_rng(11)
+    sel = routes_with_counts(counts, M, cfg.topk, rng)
+    assert [int((sel == e).sum()) for e in range(cfg.n_experts)] == counts
+    rw = (rng.random((M, cfg.topk)) + 0.1).astype(np.float32)
+    layer = make_layer(cfg, "cpu", seed=5)
+    x = torch.randn(M, cfg.hidden, generator=torch.Generator().manual_seed(12)).to(torch.bfloat16)
+    out = run(lib, "eva_moe_experts_prefill", cfg, layer.to(DEV), x.to(DEV), sel, rw)
+    ref = oracle.moe_forward(x.view(torch.int16).numpy().view(np.uint16), sel, rw, layer)
+    close(out, ref, 3e-3, 0.99999)
