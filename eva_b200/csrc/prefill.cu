@@ -167,6 +167,15 @@ __device__ __forceinline__ uint8_t* pf_ring_align(uint8_t* raw)
     return raw + ((1024 - (a & 1023)) & 1023);
 }
 
+// Store an mma.m16n8k16 A fragment (the lane's 4 registers: rows g / g + 8 x k 2t.. / 2t + 8..) as
+// its four 8 x 8 matrices; addr: this lane's row address (see the decoders).
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4])
+{
+    asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+
 // Byte offset of element (row, k) (k < 64, fp16) in a K-major 128B-swizzled 128 x 64 tile.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k)
 {
@@ -557,16 +566,15 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
         const LaneW lw = lane_w<K>(lane);
         const uint32_t ring_s = smem_u32(ring);
         // swizzled offsets of the lane's 4 words in each of its tiles (fixed for the whole loop)
-        uint32_t so[TPW][4];
+        // A tile's four 8 x 8 fragments (rows n / n + 8 x k / k + 8) go out in one stmatrix.x4: lane
+        // i gives the address of row i % 8 of fragment i / 8, a 16-byte run of the swizzled layout
+        uint32_t so[TPW];
 #pragma unroll
         for (int t = 0; t < TPW; ++t) {
-            const int n = (nt0 + t) * 16 + (lane >> 2);   // output column within the chunk (B row)
-            const int k = (ktl & 3) * 16 + 2 * (lane & 3);  // k within the 64-deep sub-tile
-            const uint32_t sub = (ktl >> 2) * PF_B_BYTES;
-            so[t][0] = sub + sw128_off(n, k);
-            so[t][1] = sub + sw128_off(n + 8, k);
-            so[t][2] = sub + sw128_off(n, k + 8);
-            so[t][3] = sub + sw128_off(n + 8, k + 8);
+            const int mi = lane >> 3;
+            const int n = (nt0 + t) * 16 + (mi & 1) * 8 + (lane & 7);   // output column within the chunk (B row)
+            const int k = (ktl & 3) * 16 + (mi >> 1) * 8;              // k within the 64-deep sub-tile
+            so[t] = (ktl >> 2) * PF_B_BYTES + sw128_off(n, k);
         }
         const uint32_t tw0 = nt0 * 32 * K + lw.w0 * 4, tw1 = nt0 * 32 * K + lw.w1 * 4;
         const uint32_t tring = ring_s + static_cast<uint32_t>(CFG::ring_bytes) + ktl * TROW;
@@ -593,9 +601,7 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
             if (L.dec_valid) {
                 const uint32_t bt = ring_s + st * PF_STAGE + A_BYTES;
 #pragma unroll
-                for (int t = 0; t < TPW; ++t)
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) sts32(bt + so[t][r], a[t][r]);
+                for (int t = 0; t < TPW; ++t) stsm_x4(bt + so[t], a[t]);
                 fence_proxy_async_smem();
             }
             __syncwarp();
