@@ -846,6 +846,8 @@ MICRO_VARIANTS = {
     16: "variant 12 with one contiguous copy per stage instead of 32 row copies",
     17: "variant 12 with one 2-D tensor copy (TMA tensor map over the strided rows) per stage",
     18: "variant 12 with the stage copied by cp.async 16-byte copies from the producer warp",
+    19: "variant 8 with the byte sum left to 8-bit MMAs: each weight's mul1 product as 4 u8 K positions, "
+        "activations as two 8-bit digits (m16n8k32 u8 x s8 and u8 x u8), 4 MMAs per tile, no dp4a or packing",
 }
 
 

@@ -27,6 +27,7 @@
 //  16  12 with one contiguous copy per stage instead of 32 row copies
 //  17  12 with one 2-D tensor copy (TMA tensor map, rows row_stride apart) per stage
 //  18  12 with the stage copied by cp.async 16-byte copies from the producer warp
+//  19  8 with the byte sum left to 8-bit MMAs (m16n8k32 u8 x s8 / u8 x u8, two activation digits)
 // eva_tc_selftest checks the TMEM layouts those designs rely on: the 16x256b store mapping, and
 // kind::i8 / kind::f16 MMAs whose A operand is read from TMEM.
 #include <cuda_runtime.h>
@@ -60,6 +61,27 @@ __device__ __forceinline__ uint32_t hash32(uint32_t x)
 
 // POL: 0 the fused kernel's decode_raw (4 words per lane-tile); 1 + (NB, PRMT) combination: the
 // two-word decode with NB windows extracted on the FMA pipe and pairs packed by PRMT or IMAD.
+// 8-bit MMAs (m16n8k32, s32 accumulate): A = the weights' mul1 products as 4 unsigned bytes each
+// (one weight per 4-byte K group), B = one 8-bit digit of a 16-bit fixed-point activation.
+__device__ __forceinline__ void mma_16832_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void mma_16832_u8u8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// POL 2: the byte sum left to 8-bit MMAs. A lane's 8 products (positions j0 (g, 2t) j1 (g, 2t+1) j2
+// (g, 2t+8) j3 (g, 2t+9), j4..j7 the same for row g + 8) fill the A fragments of two m16n8k32 MMAs
+// (k order permuted, B permuted alike), each run for the two activation digits: no dp4a, no packing.
 // STAGE: every pass also does what a stage of the fused kernel does around its tiles (B fragments of
 // the 4 rows loaded from shared memory, an mbarrier arrive and wait, a warp barrier).
 template <int K, int POL, int NB, bool PRMT, bool STAGE = false>
@@ -80,9 +102,10 @@ __global__ void __launch_bounds__(MB_DEC * 32, 1) mb_legacy(int iters, unsigned 
     const LaneGrp dg = lane_grp<K>(lane);
     const LaneW dw = lane_w<K>(lane);
     float acc[4][4] = {};
+    int iacc[4][2][4] = {};
     uint32_t b[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) b[i] = hash32(lane + 99 * i) & 0x3c003c00u;   // small fp16 values
+    for (int i = 0; i < 8; ++i) b[i] = hash32(lane + 99 * i) & (POL == 2 ? 0x7f7f7f7fu : 0x3c003c00u);
     const unsigned long long t0 = clock64();
     for (int it = 0; it < iters; ++it) {
         // a different stage quarter every pass, so the decode cannot be hoisted out of the loop
@@ -98,10 +121,22 @@ __global__ void __launch_bounds__(MB_DEC * 32, 1) mb_legacy(int iters, unsigned 
             const uint32_t* rowp = tr + (((rbase + r) & (MB_ROWS - 1)) * MB_NT + 4 * whalf) * 8 * K;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
-                uint32_t a[4];
-                if (POL == 0) decode_raw<K>(rowp + t * 8 * K, dg, a);
-                else decode_afrag_w<K, NB, PRMT>(rowp + t * 8 * K, dw, a);
-                mma_16816(acc[t], a, b[2 * r], b[2 * r + 1]);
+                if (POL == 2) {
+                    uint32_t st[8];
+                    lane_states_w<K, NB>(rowp[t * 8 * K + dw.w0], rowp[t * 8 * K + dw.w1], dw, st);
+                    uint32_t pr[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) pr[j] = st[j] * 0x83DCD12Du;
+                    mma_16832_u8s8(iacc[t][0], pr[0], pr[4], pr[1], pr[5], b[2 * r], b[2 * r + 1]);
+                    mma_16832_u8u8(iacc[t][1], pr[0], pr[4], pr[1], pr[5], b[(2 * r + 2) & 7], b[(2 * r + 3) & 7]);
+                    mma_16832_u8s8(iacc[t][0], pr[2], pr[6], pr[3], pr[7], b[(2 * r + 4) & 7], b[(2 * r + 5) & 7]);
+                    mma_16832_u8u8(iacc[t][1], pr[2], pr[6], pr[3], pr[7], b[(2 * r + 6) & 7], b[(2 * r + 7) & 7]);
+                } else {
+                    uint32_t a[4];
+                    if (POL == 0) decode_raw<K>(rowp + t * 8 * K, dg, a);
+                    else decode_afrag_w<K, NB, PRMT>(rowp + t * 8 * K, dw, a);
+                    mma_16816(acc[t], a, b[2 * r], b[2 * r + 1]);
+                }
             }
         }
         if (STAGE) {
@@ -116,7 +151,7 @@ __global__ void __launch_bounds__(MB_DEC * 32, 1) mb_legacy(int iters, unsigned 
 #pragma unroll
     for (int t = 0; t < 4; ++t)
 #pragma unroll
-        for (int c = 0; c < 4; ++c) s += acc[t][c];
+        for (int c = 0; c < 4; ++c) s += acc[t][c] + static_cast<float>(iacc[t][0][c]) + static_cast<float>(iacc[t][1][c]);
     if (s == 12345.678f) sink[0] = 1;
     if (threadIdx.x == 0) atomicMax(cyc, t1 - t0);
 }
@@ -422,7 +457,7 @@ cudaError_t run_micro(int variant, int iters, unsigned long long* cyc, int* stat
                       int sms)
 {
     static_assert(1024 + 2048 + static_cast<size_t>(MB_ROWS) * MB_NT * 8 * 4 * 4 <= MB_SMEM, "resident stage");
-    if (variant >= 12) {
+    if (variant >= 12 && variant <= 18) {
         const size_t bytes = variant == 13 ? (static_cast<size_t>(32) << 20) : (static_cast<size_t>(1) << 30);
         uint8_t* src = nullptr;
         if (cudaMallocAsync(&src, bytes + 8192, st) != cudaSuccess) return cudaErrorMemoryAllocation;
@@ -471,6 +506,7 @@ cudaError_t run_micro(int variant, int iters, unsigned long long* cyc, int* stat
             case 9: k = mb_legacy<K, 1, 2, false>; break;
             case 10: k = mb_legacy<K, 1, 4, true>; break;
             case 11: k = mb_legacy<K, 1, 2, true, true>; break;
+            case 19: k = mb_legacy<K, 2, 2, true>; break;
             default: return cudaErrorInvalidValue;
         }
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(MB_SMEM));
@@ -499,7 +535,7 @@ using namespace eva;
 
 extern "C" int eva_decode_microbench(int32_t variant, int32_t bits, int32_t iters, double* out, void* stream)
 {
-    if (!out || variant < 0 || variant > 18 || bits < 2 || bits > 4 || iters < 1 || iters > (1 << 24))
+    if (!out || variant < 0 || variant > 19 || bits < 2 || bits > 4 || iters < 1 || iters > (1 << 24))
         return EVA_ERR_INVALID;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     unsigned long long* cyc = nullptr;
@@ -528,7 +564,7 @@ extern "C" int eva_decode_microbench(int32_t variant, int32_t bits, int32_t iter
     // weights per CTA: variant 0: 16 warps x iters x 16 tiles; TMEM variants: 4 x iters slots of
     // 4 warps x 2 n-tiles x KT k-tiles (i8 KT = 4, f16 KT = 8)
     const bool i8 = variant == 1 || variant == 3 || variant == 5;
-    const bool legacy = variant == 0 || (variant >= 6 && variant <= 11);
+    const bool legacy = variant == 0 || (variant >= 6 && variant <= 11) || variant == 19;
     const double tiles = variant >= 12 ? 16.0 * iters * 16 : legacy ? 16.0 * iters * 16 : 4.0 * iters * 4 * 2 * (i8 ? 4 : 8);
     out[0] = tiles * 256.0 / static_cast<double>(h[0] ? h[0] : 1);   // weights per SM clock
     out[1] = static_cast<double>(h[0]);                               // SM clocks (max over CTAs)

@@ -355,7 +355,8 @@ int eva_host_mapped(const void* p);
  * variant 8 with a fused-kernel stage's bookkeeping around each pass; 12 / 13: variant 8 fed by
  * the fused kernel's bulk-copy ring from a 1 GB (HBM) / 32 MB (L2) source, allocated by the call;
  * 14: 5 ring stages; 15: decoders not waiting for the data; 16: one contiguous copy per stage;
- * 17: one 2-D tensor copy per stage; 18: cp.async 16-byte copies by the producer warp.
+ * 17: one 2-D tensor copy per stage; 18: cp.async 16-byte copies by the producer warp; 19: variant 8
+ * with the byte sum left to 8-bit MMAs (m16n8k32, the mul1 products as u8 A, two activation digits).
  * bits: EXL3 K (2..4).
  * out[5] = {decoded weights per SM clock, SM clocks of the launch (max over CTAs), weights decoded,
  * device status bits, event time of the launch in ms}. Synchronises the stream.

@@ -70,7 +70,7 @@ def test_umma_f16_with_a_in_tmem():
     assert np.allclose(got, want, rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("variant", list(range(19)))
+@pytest.mark.parametrize("variant", list(range(20)))
 def test_decode_microbench_runs(variant):
     lib = _lib.load()
     out = (ctypes.c_double * 5)()
