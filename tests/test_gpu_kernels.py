@@ -121,16 +121,18 @@ def test_group_limited_ties_and_masking(lib, oracle):
     assert np.array_equal(idx[0], np.arange(8))
 
 
-@pytest.mark.parametrize("x_dtype", [torch.bfloat16, torch.float16], ids=["bf16", "f16"])
-@pytest.mark.parametrize("M", [1, 5, 32, 33, 128, 200, 1000])
+# bf16 activations at every size; fp16 ones at one size per kernel path (GEMV, SIMT GEMM)
+ROUTER_CASES = [(M, torch.bfloat16) for M in (1, 5, 32, 33, 128, 200, 1000)] + [(5, torch.float16), (200, torch.float16)]
+
+
+@pytest.mark.parametrize("M,x_dtype", ROUTER_CASES,
+                         ids=[f"{m}-{'bf16' if d == torch.bfloat16 else 'f16'}" for m, d in ROUTER_CASES])
 @pytest.mark.parametrize("cfg", [C.V3, C.V2_LITE], ids=lambda c: c.name)
 def test_router_logits_and_indices(lib, oracle, cfg, M, x_dtype):
     """M <= 32: k-sliced GEMV; larger bf16 batches: the tensor-core GEMM (three bf16 parts of each
     FP32 weight, k slices summed by the top-k kernel); larger fp16 batches: the SIMT GEMM.
     V2-Lite at 128 tokens is the router half of the FP32 CPU case: dense N(0, 0.02) router weights
     from seed 0, N(0, 1) hidden states, softmax top-6."""
-    if x_dtype == torch.float16 and M not in (5, 200):
-        pytest.skip("fp16 activations: one size per path")
     layer = make_layer(cfg.with_(n_experts=cfg.n_experts), "cpu", seed=0, n_fill=0)
     g = torch.Generator().manual_seed(1)
     x = torch.randn(M, cfg.hidden, generator=g).to(torch.bfloat16).to(x_dtype)
