@@ -20,7 +20,7 @@ from eva_b200 import config as C
 from eva_b200.experts import make_layer
 
 DEV = "cuda"
-# largest accepted rows per call (documented in include/eva_moe.h, DESIGN.md and INTEGRATION.md)
+# largest accepted rows per call (documented in include/eva_moe.h beside the entry point)
 MAX_ROWS = {"v3": 28, "v2-lite": 90, "ref-native": 47}
 
 
