@@ -173,22 +173,46 @@ def _free_port():
         return s.getsockname()[1]
 
 
+def _run_ranks(n, args):
+    """tests/ep_worker.py on n ranks under torch.distributed.run; a new rendezvous port when the chosen
+    one was taken between choosing and binding it (EADDRINUSE), up to three tries."""
+    for _ in range(3):
+        cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+               f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", f"--master-port={_free_port()}",
+               str(ROOT / "tests" / "ep_worker.py"), *args]
+        r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=400)
+        if r.returncode == 0 or "EADDRINUSE" not in r.stderr + r.stdout:
+            return r
+    return r
+
+
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("transport,mode,M", [("peers", "fixed", 8), ("peers", "exact", 700), ("nccl", "fixed", 8),
                                               ("nccl", "exact", 700)])
 def test_ep_ranks_match_one_gpu(tmp_path, transport, mode, M):
     n = min(torch.cuda.device_count(), 4)
     out = tmp_path / "ep.json"
-    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={n}", "--master-addr", "127.0.0.1", f"--master-port={_free_port()}",
-           str(ROOT / "tests" / "ep_worker.py"), "--mode", mode, "--transport", transport, "--tokens", str(M),
-           "--out", str(out)]
-    r = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=400)
+    r = _run_ranks(n, ["--mode", mode, "--transport", transport, "--tokens", str(M), "--out", str(out)])
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads(out.read_text())
     assert res["status"] == 0
     # 700 tokens: a rank may take the register-decode kernel where the whole layer takes the tensor-core one
     assert res["max_rel_err"] < (1e-4 if M <= 64 else 3e-3), res
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_ranks_with_device_expert_cache_match_one_gpu(tmp_path):
+    """Two layers per rank behind one device expert pool smaller than their experts (evictions,
+    prefetches of the other layer, split launches around the misses' copies) over the peer-memory
+    transport: every step of both layers equals the whole layers on one GPU."""
+    n = min(torch.cuda.device_count(), 4)
+    out = tmp_path / "ep_pool.json"
+    r = _run_ranks(n, ["--pool", "--tokens", "8", "--out", str(out)])
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    res = json.loads(out.read_text())
+    assert res["status"] == 0
+    assert all(c > 0 for c in res["pool_bytes_copied"])
+    assert res["max_rel_err"] < 1e-4, res
 
 
 @pytest.mark.parametrize("M,row0,rows", [(40, 8, 17), (300, 64, 150), (300, 0, 0)])
