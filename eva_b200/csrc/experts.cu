@@ -13,9 +13,10 @@
 // waits on anything but its own CTA's partial sums.
 //
 // Per CTA (warp specialised):
-//   warp 16      producer: claims items and streams their trellis rows with 1-D bulk copies (TMA,
-//                one CTA per copy) into a 4-stage shared-memory ring (32 k-tile rows x 128 columns
-//                per stage), writing each item's geometry, run and slots into the stage header
+//   warp 16      producer: claims items and streams each stage of their trellis rows (32 k-tile rows x
+//                128 columns) with one 2-D TMA tensor copy into a shared-memory ring (5 stages when the
+//                launch's widest trellis is K <= 3, else 4), writing each item's geometry, run and slots
+//                into the stage header; warp 21 copies the run's B rows of each stage
 //   warps 0..15  decoders: each decodes 4 rows x 4 tiles per stage in registers (two words and two
 //                funnel shifts per lane and tile, window extraction split between the ALU and FMA
 //                pipes) and runs mma.m16n8k16 with the weights as the 16 x 16 A operand (rows =
@@ -46,16 +47,25 @@ constexpr int NCW = 16;                    // decoding warps (warps 0..15)
 constexpr int NEW = 4;                     // epilogue warps (warps 17..20; warp 16 is the trellis producer)
 constexpr int BPW = NCW + 1 + NEW;         // the B producer warp (21)
 constexpr int THREADS = (NCW + 2 + NEW) * 32;
-constexpr int NSTAGE = 4;
 constexpr int STAGE_KT = 32;               // k-tile rows per stage (4 per decoding warp pair)
 constexpr int NT = 8;                      // 16-column tiles per item (128 output columns)
-constexpr int STAGE_BYTES = STAGE_KT * NT * 32 * 4;   // trellis of a stage, sized for K = 4
 constexpr int BROW_BYTES = STAGE_KT * 32;              // one token row of B for the stage's k-tile rows (fp16)
-constexpr int STAGE_TOTAL = STAGE_BYTES + RUN_ROWS * BROW_BYTES;   // + the run's 8 B rows
 constexpr int RES_FLOATS = 2 * RUN_ROWS * 128;
 constexpr int PART_F4 = NCW * 4 * 32;      // one projection's partial sums: [warp][tile][lane] float4
-constexpr size_t SMEM_BYTES =
-    static_cast<size_t>(NSTAGE) * STAGE_TOTAL + PART_F4 * 16 + RES_FLOATS * 4 + (3 * NSTAGE + 2) * 8;
+
+// The ring of a launch whose largest trellis width is KMAX: stages sized for KMAX, and one stage more
+// where that leaves room (K <= 3), so the copies run further ahead of the decoders.
+template <int KMAX>
+struct DecRing {
+    static constexpr int nstage = KMAX <= 3 ? 5 : 4;
+    static constexpr int stage_bytes = STAGE_KT * NT * 32 * KMAX;
+    static constexpr int stage_total = stage_bytes + RUN_ROWS * BROW_BYTES;
+    static constexpr size_t smem =
+        static_cast<size_t>(nstage) * stage_total + PART_F4 * 16 + RES_FLOATS * 4 + (3 * nstage + 2) * 8;
+    static_assert(nstage + 1 <= DEC_MAP_SETS, "an item's tensor-map set is reused only after nstage + 1 items");
+    static_assert(stage_total % 1024 == 0, "stage alignment");
+};
+constexpr int DEC_NSTAGE_MAX = 5;
 
 struct KParams {
     // shape
@@ -436,6 +446,9 @@ struct TrellisMaps {
 template <int KR, int KS>
 __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, const __grid_constant__ TrellisMaps tm)
 {
+    using R = DecRing<(KR > KS ? KR : KS)>;
+    constexpr int NSTAGE = R::nstage, STAGE_BYTES = R::stage_bytes, STAGE_TOTAL = R::stage_total;
+    static_assert(NSTAGE <= DEC_NSTAGE_MAX, "stage headers");
     extern __shared__ __align__(1024) uint8_t smem[];
     uint32_t* ring = reinterpret_cast<uint32_t*>(smem);
     float4* part = reinterpret_cast<float4*>(smem + static_cast<size_t>(NSTAGE) * STAGE_TOTAL);   // [warp][t][lane]
@@ -446,7 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, co
     uint64_t* hready = empty + NSTAGE;     // the stage header is written (trellis producer -> B producer)
     uint64_t* pfull = hready + NSTAGE;     // decoders -> epilogue warps: one projection's partial sums written
     uint64_t* pfree = pfull + 1;           // epilogue warps -> decoders: partial sums consumed
-    __shared__ StageHdr hdr[NSTAGE];
+    __shared__ StageHdr hdr[DEC_NSTAGE_MAX];
     __shared__ PartInfo pinfo;
     __shared__ PartInfo epi;               // the epilogue warps' copy of the item they finish
     __shared__ WarpItem wi0;               // decoder warp 0's copy of its current item
@@ -914,9 +927,11 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
         return cudaErrorInvalidValue;
     const ExpertsKernel kern = pick_kernel(p.K, p.K_sh);
     if (!kern) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(SMEM_BYTES));
+    const int kmax = std::max(p.K, p.K_sh);
+    const size_t smem = kmax <= 2 ? DecRing<2>::smem : (kmax == 3 ? DecRing<3>::smem : DecRing<4>::smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kern<<<std::min(sms, DEC_MAX_CTAS), THREADS, SMEM_BYTES, stream>>>(p, tm);
+    kern<<<std::min(sms, DEC_MAX_CTAS), THREADS, smem, stream>>>(p, tm);
     return cudaGetLastError();
 }
 

@@ -100,7 +100,7 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream);
 cudaError_t launch_prefill(const ExpertsArgs& a, cudaStream_t stream);
 
 constexpr int DEC_MAX_CTAS = 256;       // decode kernel grid cap (tensor-map slots per CTA in the workspace)
-constexpr int DEC_MAP_SETS = 5;         // tensor-map sets per CTA: one per item, reused after NSTAGE + 1 items
+constexpr int DEC_MAP_SETS = 6;         // tensor-map sets per CTA: one per item, reused after (ring stages + 1) items
 constexpr int PREFILL_MIN_ROWS = 129;   // eva_moe_experts takes the tensor-core path from this many rows
 constexpr int PF_TILE_ROWS = 256;       // rows of one expert per tensor-core CTA (two 128-row MMA halves)
 

@@ -167,7 +167,7 @@ int eva_exl3_dequant(const void* trellis, int32_t in_features, int32_t out_featu
  * cudaMalloc because it can synchronise the device. The caller passes inputs and outputs exactly as
  * for eva_moe_experts; the scratch is a file-scope device array of EVA_NOALLOC_SCRATCH_BYTES.
  *   - Calls whose scratch would exceed that size are rejected with EVA_ERR_WORKSPACE (for the
- *     DeepSeek-V3 shape this allows up to 28 tokens per call, DeepSeek-V2-Lite 90, eva's own
+ *     DeepSeek-V3 shape this allows up to 27 tokens per call, DeepSeek-V2-Lite 90, eva's own
  *     H5120 / 384-expert shape 47). Every call takes the decode kernel, whatever its row count.
  *   - Argument errors (EVA_ERR_INVALID) and the size check (EVA_ERR_WORKSPACE) are reported before
  *     any device call.
