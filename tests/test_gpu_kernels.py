@@ -268,10 +268,12 @@ def _run_experts(lib, cfg, layer_d, x, sel, rw, shared=True, limit=None, act_rou
     return out.cpu().numpy(), outb.float().cpu().numpy(), st.value
 
 
-@pytest.mark.parametrize("bits", [2, 3, 4])
+@pytest.mark.parametrize("bits,shared_bits", [(2, 4), (3, 4), (4, 4), (2, 2), (3, 3)])
 @pytest.mark.parametrize("M", [1, 3, 8, 13])
-def test_experts_small(lib, oracle, bits, M):
-    cfg = SMALL.with_(bits=bits)
+def test_experts_small(lib, oracle, bits, shared_bits, M):
+    """Routed and shared trellis widths: the ring's stages are sized for the widest of the launch
+    (5 stages when both are K <= 3, 4 with a K = 4 projection)."""
+    cfg = SMALL.with_(bits=bits, shared_bits=shared_bits)
     layer = make_layer(cfg, "cpu", seed=bits)
     layer_d = layer.to(DEV)
     rng = np.random.default_rng(M * 10 + bits)
