@@ -16,7 +16,7 @@
 //   warp 16      producer: claims items and streams each stage of their trellis rows (32 k-tile rows x
 //                128 columns) with one 2-D TMA tensor copy into a shared-memory ring (5 stages when the
 //                launch's widest trellis is K <= 3, else 4), writing each item's geometry, run and slots
-//                into the stage header; warp 21 copies the run's B rows of each stage
+//                into the stage header; warp 19 copies the run's B rows of each stage
 //   warps 0..15  decoders: each decodes 4 rows x 4 tiles per stage in registers (two words and two
 //                funnel shifts per lane and tile, window extraction split between the ALU and FMA
 //                pipes) and runs mma.m16n8k16 with the weights as the 16 x 16 A operand (rows =
@@ -24,7 +24,7 @@
 //                raw codebook values h = 1024 + bytesum and the codebook's affine map is applied to
 //                the sums (see decode_raw). At a projection's end they store their partial sums
 //                and go straight on; rotation items are done by these 16 warps together.
-//   warps 17..20 epilogue: sum the 8 k-quads of a projection's partials (mbarrier hand-off, the
+//   warps 17..18 epilogue: sum the 8 k-quads of a projection's partials (mbarrier hand-off, the
 //                partial buffer is released right after), then the item's epilogue (split-k
 //                publication, Hadamard / scales / activation or the combine) while the decoders
 //                already run the next item.
@@ -44,8 +44,8 @@
 namespace eva {
 
 constexpr int NCW = 16;                    // decoding warps (warps 0..15)
-constexpr int NEW = 4;                     // epilogue warps (warps 17..20; warp 16 is the trellis producer)
-constexpr int BPW = NCW + 1 + NEW;         // the B producer warp (21)
+constexpr int NEW = 2;                     // epilogue warps (warps 17..18; warp 16 is the trellis producer)
+constexpr int BPW = NCW + 1 + NEW;         // the B producer warp (19)
 constexpr int THREADS = (NCW + 2 + NEW) * 32;
 constexpr int STAGE_KT = 32;               // k-tile rows per stage (4 per decoding warp pair)
 constexpr int NT = 8;                      // 16-column tiles per item (128 output columns)
