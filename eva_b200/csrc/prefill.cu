@@ -782,9 +782,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PfGateCfg::threads, 
     __shared__ float rsum[2][PF_BM];
     {
         const int nchH = p.H / 128;
-        if (threadIdx.x < PF_BM * 4) {
-            pf_row_sums<4>(p.xsum, nchH, nchH, L.row0, rows, rsum[0], PF_BM * 4);
-            pf_row_sums<4>(p.xsum + (static_cast<size_t>(p.S_cap) + p.M) * nchH, nchH, nchH, L.row0, rows, rsum[1], PF_BM * 4);
+        constexpr int RS_THREADS = PF_THREADS < PF_BM * 4 ? PF_THREADS : PF_BM * 4;   // the threads that gather
+        if (threadIdx.x < RS_THREADS) {
+            pf_row_sums<4>(p.xsum, nchH, nchH, L.row0, rows, rsum[0], RS_THREADS);
+            pf_row_sums<4>(p.xsum + (static_cast<size_t>(p.S_cap) + p.M) * nchH, nchH, nchH, L.row0, rows, rsum[1], RS_THREADS);
         }
     }
     for (int c = 0; c < 2; ++c) {
