@@ -269,7 +269,9 @@ __device__ __forceinline__ void gemv_row_w(uint32_t tiles, const LaneW& d, uint3
 #pragma unroll
     for (int t = 0; t < WT; ++t) {
         uint32_t a[4];
-        decode_afrag_ww<K, 2, true>(w[t][0], w[t][1], d, a);
+        // 4 of the 8 windows extracted and, below K = 4, the pairs packed on the FMA pipe: the ALU pipe
+        // is the busier one in this kernel (measured best: 2 or 6 windows, or byte-permute packs, are slower)
+        decode_afrag_ww<K, 4, (K == 4)>(w[t][0], w[t][1], d, a);
         mma_16816(acc[t], a, b0, b1);
     }
 }
