@@ -590,9 +590,10 @@ __device__ __forceinline__ void pf_mainloop(const PfLoop& L, uint8_t* ring, PfBa
                     w[t][0] = lds32(tr + t * 32 * K + tw0);
                     w[t][1] = lds32(tr + t * 32 * K + tw1);
                 }
-                // two-word decode, 2 windows extracted on the FMA pipe, pairs packed by byte permutes
+                // two-word decode, 4 windows extracted on the FMA pipe and, below K = 4, pairs packed
+                // by integer multiply-adds (the ALU pipe carries the rest of the decode)
 #pragma unroll
-                for (int t = 0; t < TPW; ++t) decode_afrag_ww<K, 2, true>(w[t][0], w[t][1], lw, a[t]);
+                for (int t = 0; t < TPW; ++t) decode_afrag_ww<K, 4, (K == 4)>(w[t][0], w[t][1], lw, a[t]);
             }
             // the words are in registers (the decode consumed them): release the trellis slot
             __syncwarp();
