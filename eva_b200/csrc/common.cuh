@@ -160,31 +160,43 @@ __device__ __forceinline__ void named_sync(int id, int threads)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Packed fp32 pairs (sm_100's two-wide FADD / FMUL / FFMA): each half is rounded exactly as the
+// scalar operation rounds it, so a butterfly written on pairs gives the scalar code's bits with
+// half the instructions. a - b is fma(b, -1, a): the product is exact, the one rounding is a - b's.
+
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.0f, -1.0f), a); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+
+// ---------------------------------------------------------------------------------------------
 // 128-point Hadamard across a warp: lane l holds elements 4l..4l+3. Natural (Sylvester) order,
 // scaled by 1/sqrt(128): out[i] = sum_j (-1)^popcount(i & j) in[j] / sqrt(128).
 
 __device__ __forceinline__ void had128_warp(float (&v)[4], int lane)
 {
-    // in-register butterflies over the two low index bits
-    float a = v[0] + v[1], b = v[0] - v[1], c = v[2] + v[3], d = v[2] - v[3];
-    v[0] = a + c;
-    v[1] = b + d;
-    v[2] = a - c;
-    v[3] = b - d;
+    // in-register butterflies over the two low index bits: bit 0 inside the pairs (v0, v1) and
+    // (v2, v3), bit 1 between the pairs as packed operations
+    const float2 p = make_float2(v[0] + v[1], v[0] - v[1]), q = make_float2(v[2] + v[3], v[2] - v[3]);
+    float2 lo = add2(p, q), hi = sub2(p, q);   // new (v0, v1) = p + q, new (v2, v3) = p - q
     // butterflies over the 5 lane bits: lower lane v + o, upper lane o - v, both as one fma with the
     // lane's sign (exactly the same roundings as the add / subtract)
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-        const float sg = (lane & m) ? -1.0f : 1.0f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
-            v[i] = __fmaf_rn(v[i], sg, o);
-        }
+        const float s1 = (lane & m) ? -1.0f : 1.0f;
+        const float2 sg = make_float2(s1, s1);
+        const float2 olo = make_float2(__shfl_xor_sync(0xffffffffu, lo.x, m), __shfl_xor_sync(0xffffffffu, lo.y, m));
+        const float2 ohi = make_float2(__shfl_xor_sync(0xffffffffu, hi.x, m), __shfl_xor_sync(0xffffffffu, hi.y, m));
+        lo = fma2(lo, sg, olo);
+        hi = fma2(hi, sg, ohi);
     }
-    const float s = 0.08838834764831845f;   // 1/sqrt(128)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] *= s;
+    const float2 s = make_float2(0.08838834764831845f, 0.08838834764831845f);   // 1/sqrt(128)
+    lo = mul2(lo, s);
+    hi = mul2(hi, s);
+    v[0] = lo.x;
+    v[1] = lo.y;
+    v[2] = hi.x;
+    v[3] = hi.y;
 }
 
 // Explicit shared-space accesses for decoding warps (generic accesses wait on the long scoreboard).

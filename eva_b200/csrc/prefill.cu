@@ -322,7 +322,9 @@ __device__ __forceinline__ int pf_row_slot(const PfParams& p, int pos)
 // and stores are contiguous 64-byte runs per chunk. The 128-point Hadamard transform takes its
 // butterflies in the order of the index bits, 0 to 6, as had128_warp does (bits 0-2 and 5-6 in
 // registers, bits 3-4 by two shuffles): the same operations, so the same fp32 results, with 2
-// shuffle stages per 32 values instead of 5 per 4.
+// shuffle stages per 32 values instead of 5 per 4. The lane's values are held as packed pairs
+// (elements 2k, 2k + 1): every butterfly level but bit 0's, the input scaling and the output
+// scaling take one two-wide instruction per pair.
 
 // 8 consecutive activations (bf16 or fp16) as floats; al16: the address is 16-byte aligned
 __device__ __forceinline__ void load8_x(const void* x, size_t off, int is_bf16, bool al16, float (&v)[8])
@@ -354,7 +356,9 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
     const int lane = threadIdx.x & 31, q = lane >> 2, r = lane & 3;
     const int n_act = p.runs[2 + p.runs[0]];
     const int n_rows = n_act + (p.has_shared ? p.shn : 0);
-    const int nch = p.H / 128;
+    const unsigned nch = static_cast<unsigned>(p.H / 128);
+    // rows x chunks of one projection stay below 2^32: each (row, chunk) owns 512 bytes of rotated
+    // activations in the workspace, so 2^32 of them would be 2 TB
     const long long per_proj = static_cast<long long>(n_rows) * nch;
     const long long n_units = 2 * per_proj;   // (projection, row, chunk), chunk fastest
     const bool al16 = (reinterpret_cast<uintptr_t>(p.x) & 15) == 0;
@@ -363,14 +367,15 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
          u0 += warps * 8) {
         const long long u = u0 + q;
         const bool valid = u < n_units;   // the lanes of a past-the-end chunk still take part in the shuffles
-        float v[32];
+        // v[k] holds elements 2k, 2k + 1 of the lane's 32 (index i = 8 j + e): packed pairs
+        float2 v[16];
         int pj = 0, pos = 0, c = 0;
         if (valid) {
             pj = u >= per_proj;
-            const long long rem = u - pj * per_proj;
-            const int row = static_cast<int>(rem / nch);
-            c = static_cast<int>(rem - static_cast<long long>(row) * nch);
-            pos = row < n_act ? row : p.S_cap + p.sh0 + (row - n_act);
+            const unsigned rem = static_cast<unsigned>(u - pj * per_proj);
+            const unsigned row = rem / nch;
+            c = static_cast<int>(rem - row * nch);
+            pos = static_cast<int>(row) < n_act ? static_cast<int>(row) : p.S_cap + p.sh0 + (static_cast<int>(row) - n_act);
             int tok;
             const __half* suh;
             if (pos >= p.S_cap) {
@@ -391,62 +396,68 @@ __global__ void __launch_bounds__(256) pf_rotate(const PfParams p)
                 const uint4 su = __ldg(reinterpret_cast<const uint4*>(sp + j * 32));
                 const uint32_t sw[4] = {su.x, su.y, su.z, su.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const __half2 h = *reinterpret_cast<const __half2*>(&sw[i]);
-                    v[j * 8 + 2 * i] = xv[2 * i] * __low2float(h);
-                    v[j * 8 + 2 * i + 1] = xv[2 * i + 1] * __high2float(h);
-                }
+                for (int i = 0; i < 4; ++i)
+                    v[j * 4 + i] = mul2(make_float2(xv[2 * i], xv[2 * i + 1]),
+                                        __half22float2(*reinterpret_cast<const __half2*>(&sw[i])));
             }
         } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+            for (int k = 0; k < 16; ++k) v[k] = make_float2(0.0f, 0.0f);
         }
-        // index bits 0-2: e
+        // index bit 0: inside the pairs
 #pragma unroll
-        for (int h = 1; h < 8; h <<= 1)
+        for (int k = 0; k < 16; ++k) v[k] = make_float2(v[k].x + v[k].y, v[k].x - v[k].y);
+        // index bits 1-2 (the rest of e): between pairs k and k + h
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if ((i & h) == 0) {
-                    const float a = v[i], b = v[i + h];
-                    v[i] = a + b;
-                    v[i + h] = a - b;
+        for (int h = 1; h < 4; h <<= 1)
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                if ((k & h) == 0) {
+                    const float2 a = v[k], b = v[k + h];
+                    v[k] = add2(a, b);
+                    v[k + h] = sub2(a, b);
                 }
         // index bits 3-4: r (lane bits 0-1)
 #pragma unroll
         for (int m = 1; m < 4; m <<= 1) {
-            const float sg = (r & m) ? -1.0f : 1.0f;   // upper lane o - v, lower v + o, as one fma
+            const float s1 = (r & m) ? -1.0f : 1.0f;   // upper lane o - v, lower v + o, as one fma
+            const float2 sg = make_float2(s1, s1);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float o = __shfl_xor_sync(0xffffffffu, v[i], m);
-                v[i] = __fmaf_rn(v[i], sg, o);
+            for (int k = 0; k < 16; ++k) {
+                const float2 o =
+                    make_float2(__shfl_xor_sync(0xffffffffu, v[k].x, m), __shfl_xor_sync(0xffffffffu, v[k].y, m));
+                v[k] = fma2(v[k], sg, o);
             }
         }
         // index bits 5-6: j
 #pragma unroll
-        for (int h = 8; h < 32; h <<= 1)
+        for (int h = 4; h < 16; h <<= 1)
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if ((i & h) == 0) {
-                    const float a = v[i], b = v[i + h];
-                    v[i] = a + b;
-                    v[i + h] = a - b;
+            for (int k = 0; k < 16; ++k)
+                if ((k & h) == 0) {
+                    const float2 a = v[k], b = v[k + h];
+                    v[k] = add2(a, b);
+                    v[k + h] = sub2(a, b);
                 }
-        float sm = 0.0f;   // sum of the values as stored (fp16), for the raw-codebook correction
+        // sums of the values as stored (fp16), for the raw-codebook correction: even and odd
+        // elements accumulated as a pair, then added
+        float2 sm2 = make_float2(0.0f, 0.0f);
         if (valid) {
-            const float sc = 0.08838834764831845f;   // 1/sqrt(128)
+            const float2 sc = make_float2(0.08838834764831845f, 0.08838834764831845f);   // 1/sqrt(128)
             __half* dst = (pj ? p.xu : p.xg) + static_cast<size_t>(pos) * p.H + c * 128 + r * 8;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 uint32_t w[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const __half2 h = __floats2half2_rn(v[j * 8 + 2 * i] * sc, v[j * 8 + 2 * i + 1] * sc);
+                    const __half2 h = __float22half2_rn(mul2(v[j * 4 + i], sc));
                     w[i] = *reinterpret_cast<const uint32_t*>(&h);
-                    sm += __low2float(h) + __high2float(h);
+                    sm2 = add2(sm2, __half22float2(h));
                 }
                 *reinterpret_cast<uint4*>(dst + j * 32) = make_uint4(w[0], w[1], w[2], w[3]);
             }
         }
+        float sm = sm2.x + sm2.y;
         sm += __shfl_xor_sync(0xffffffffu, sm, 1);
         sm += __shfl_xor_sync(0xffffffffu, sm, 2);
         if (valid && r == 0) p.xsum[(static_cast<size_t>(pj) * (p.S_cap + p.M) + pos) * nch + c] = sm;
