@@ -16,7 +16,7 @@
 //   warp 16      producer: claims items and streams each stage of their trellis rows (32 k-tile rows x
 //                128 columns) with one 2-D TMA tensor copy into a shared-memory ring (5 stages when the
 //                launch's widest trellis is K <= 3, else 4), writing each item's geometry, run and slots
-//                into the stage header; warp 19 copies the run's B rows of each stage
+//                into the stage header; the last warp copies the run's B rows of each stage
 //   warps 0..15  decoders: each decodes 4 rows x 4 tiles per stage in registers (two words and two
 //                funnel shifts per lane and tile, window extraction split between the ALU and FMA
 //                pipes) and runs mma.m16n8k16 with the weights as the 16 x 16 A operand (rows =
@@ -24,10 +24,10 @@
 //                raw codebook values h = 1024 + bytesum and the codebook's affine map is applied to
 //                the sums (see decode_raw). At a projection's end they store their partial sums
 //                and go straight on; rotation items are done by these 16 warps together.
-//   warps 17..18 epilogue: sum the 8 k-quads of a projection's partials (mbarrier hand-off, the
-//                partial buffer is released right after), then the item's epilogue (split-k
-//                publication, Hadamard / scales / activation or the combine) while the decoders
-//                already run the next item.
+//   warps 17..   epilogue (2, or 4 for short or split items): sum the 8 k-quads of a projection's
+//                partials (mbarrier hand-off, the partial buffer is released right after), then the
+//                item's epilogue (split-k publication, Hadamard / scales / activation or the
+//                combine) while the decoders already run the next item.
 //
 // Reference behaviour (paths within Findddx/eva, runtime/ds41/csrc/moe_coop2048/vendor/quant/):
 //   exl3_moe_coop_kernel.cuh:634-671 (rotation), :680-809 (gate/up GEMV + epilogue),
@@ -44,9 +44,18 @@
 namespace eva {
 
 constexpr int NCW = 16;                    // decoding warps (warps 0..15)
-constexpr int NEW = 2;                     // epilogue warps (warps 17..18; warp 16 is the trellis producer)
-constexpr int BPW = NCW + 1 + NEW;         // the B producer warp (19)
-constexpr int THREADS = (NCW + 2 + NEW) * 32;
+// Epilogue warps (warps 17 .. 16 + NEW; warp 16 is the trellis producer, warp 17 + NEW the B
+// producer): 2 where items are long (a gate/up item spans more than 4096 input columns), so the
+// decoders keep more of the SM's issue slots; 4 where they are short or split (per item the
+// epilogue warps' share, the split-k reduction and the rows' epilogues, is then larger).
+// Measured (experts launch): V3 batch 8 0.569 ms with 2 vs 0.579 with 4; V3 batch 1 (split 2)
+// 0.144 vs 0.132; V2-Lite (H 2048) batch 16 0.148 vs 0.140.
+template <int NEW>
+struct DecWarps {
+    static constexpr int bpw = NCW + 1 + NEW;              // the B producer warp
+    static constexpr int threads = (NCW + 2 + NEW) * 32;
+};
+constexpr int DEC_SHORT_ITEM_COLS = 4096;  // gate/up input columns per item at or below which NEW = 4
 constexpr int STAGE_KT = 32;               // k-tile rows per stage (4 per decoding warp pair)
 constexpr int NT = 8;                      // 16-column tiles per item (128 output columns)
 constexpr int BROW_BYTES = STAGE_KT * 32;              // one token row of B for the stage's k-tile rows (fp16)
@@ -445,9 +454,11 @@ struct TrellisMaps {
     CUtensorMap gu, dn, sgu, sdn;
 };
 
-template <int KR, int KS>
-__global__ void __launch_bounds__(THREADS, 1) experts_kernel(const KParams p, const __grid_constant__ TrellisMaps tm)
+template <int KR, int KS, int NEW>
+__global__ void __launch_bounds__(DecWarps<NEW>::threads, 1)
+    experts_kernel(const KParams p, const __grid_constant__ TrellisMaps tm)
 {
+    constexpr int BPW = DecWarps<NEW>::bpw;
     using R = DecRing<(KR > KS ? KR : KS)>;
     constexpr int NSTAGE = R::nstage, STAGE_BYTES = R::stage_bytes, STAGE_TOTAL = R::stage_total;
     static_assert(NSTAGE <= DEC_NSTAGE_MAX, "stage headers");
@@ -849,10 +860,11 @@ static bool encode_trellis_map(CUtensorMap* m, void* base, int in, int out, int 
            CUDA_SUCCESS;
 }
 
+template <int NEW>
 static ExpertsKernel pick_kernel(int kr, int ks)
 {
 #define EVA_K(a, b) \
-    if (kr == a && ks == b) return experts_kernel<a, b>;
+    if (kr == a && ks == b) return experts_kernel<a, b, NEW>;
     EVA_K(2, 2) EVA_K(2, 3) EVA_K(2, 4) EVA_K(3, 2) EVA_K(3, 3) EVA_K(3, 4) EVA_K(4, 2) EVA_K(4, 3) EVA_K(4, 4)
 #undef EVA_K
     return nullptr;
@@ -927,13 +939,15 @@ cudaError_t launch_experts(const ExpertsArgs& a, cudaStream_t stream)
     if (!encode_trellis_map(&tm.gu, ws, p.H, p.I, p.K) || !encode_trellis_map(&tm.dn, ws, p.I, p.H, p.K) ||
         !encode_trellis_map(&tm.sgu, ws, p.H, ish, p.K_sh) || !encode_trellis_map(&tm.sdn, ws, ish, p.H, p.K_sh))
         return cudaErrorInvalidValue;
-    const ExpertsKernel kern = pick_kernel(p.K, p.K_sh);
+    const bool short_items = s.hidden / split <= DEC_SHORT_ITEM_COLS;
+    const ExpertsKernel kern = short_items ? pick_kernel<4>(p.K, p.K_sh) : pick_kernel<2>(p.K, p.K_sh);
+    const int threads = short_items ? DecWarps<4>::threads : DecWarps<2>::threads;
     if (!kern) return cudaErrorInvalidValue;
     const int kmax = std::max(p.K, p.K_sh);
     const size_t smem = kmax <= 2 ? DecRing<2>::smem : (kmax == 3 ? DecRing<3>::smem : DecRing<4>::smem);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    kern<<<std::min(sms, DEC_MAX_CTAS), THREADS, smem, stream>>>(p, tm);
+    kern<<<std::min(sms, DEC_MAX_CTAS), threads, smem, stream>>>(p, tm);
     return cudaGetLastError();
 }
 

@@ -49,7 +49,10 @@ __device__ __forceinline__ int block_scan01(int flag, int* warp_sums, int* total
     return before + in_warp;
 }
 
-// state: [0] hand, [1] counter (plan calls), [2] status, [3] unused; [4..5] int64 bytes copied
+// state (int32 words): [0] hand, [1] unused, [2] status, [3] unused; [4..5] int64 bytes copied;
+// [6..7] int64 plan counter. Stamps and the counter are 64-bit: one exact plan per layer per step
+// would take a 32-bit counter past 2^31 within hours of serving a 58-layer model, after which
+// "stamped before `protect`" would no longer mean "older".
 //
 // The plan is the sequential CLOCK walk (misses in expert order, each taking the next slot from the
 // hand that is free or stamped before `protect`) computed in parallel: a slot taken by one miss
@@ -96,9 +99,10 @@ __global__ void __launch_bounds__(PLAN_THREADS) pool_plan_kernel(EvaExpertPool p
     int* st = pool.state;
     // exact plan: a new stamp, protecting what it stamps now; prefetch (issued after the plan of the
     // layer that runs meanwhile): the next stamp, protecting that layer's slots too
-    const int cur = st[1];
-    const int stamp = cur + 1;
-    const int protect = prefetch ? cur : stamp;
+    long long* counter = reinterpret_cast<long long*>(st + 6);
+    const long long cur = *counter;
+    const long long stamp = cur + 1;
+    const long long protect = prefetch ? cur : stamp;
     const int hand = st[0];
     const int n = pool.n_slots;
     // hits stamped first, so that every needed resident slot is protected before any eviction; the
@@ -170,7 +174,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) pool_plan_kernel(EvaExpertPool p
         }
     }
     if (t == 0) {
-        if (!prefetch) st[1] = stamp;
+        if (!prefetch) *counter = stamp;
         if (n_take < n_miss && !prefetch) atomicOr(&st[2], ST_CAPACITY);   // the pool is smaller than a layer
         if (n_take > 0) st[0] = take_pos[n_take - 1] + 1 + hand >= n ? take_pos[n_take - 1] + 1 + hand - n
                                                                      : take_pos[n_take - 1] + 1 + hand;

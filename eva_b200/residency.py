@@ -198,7 +198,8 @@ class ExpertPool:
         self.n_slots, self.record_bytes, self.max_layers = int(n_slots), int(record_bytes), int(max_layers)
         self.slots = torch.empty(self.n_slots * self.record_bytes, dtype=torch.uint8, device=self.device)
         self.owner = torch.full((self.n_slots,), -1, dtype=torch.int32, device=self.device)
-        self.stamp = torch.zeros(self.n_slots, dtype=torch.int32, device=self.device)
+        self.stamp = torch.zeros(self.n_slots, dtype=torch.int64, device=self.device)
+        # {hand, 0, status bits, 0, bytes copied (int64), plan counter (int64)}
         self.state = torch.zeros(8, dtype=torch.int32, device=self.device)
         self._layer_bytes = ctypes.sizeof(_lib.EvaPoolLayer)
         self.layers_dev = torch.zeros(self.max_layers * self._layer_bytes, dtype=torch.uint8, device=self.device)
@@ -225,6 +226,10 @@ class ExpertPool:
     def bytes_copied(self) -> int:
         """Record bytes the copies moved so far (reads the device counter: synchronises)."""
         return int(self.state[4:6].cpu().view(torch.int64).item())
+
+    def plan_counter(self) -> int:
+        """Exact plans so far (the stamp of the latest one; reads the device counter: synchronises)."""
+        return int(self.state[6:8].cpu().view(torch.int64).item())
 
     def status(self) -> int:
         return int(self.state[2].item())

@@ -296,8 +296,9 @@ int32_t eva_moe_arch(void);
  * addresses. Nothing synchronises the host.
  *
  * EvaExpertPool (device arrays): slots n_slots * record_bytes; owner [n_slots] (layer << 16 | expert,
- *   -1 free); stamp [n_slots]; state int32 [6] = {hand, plan counter, status bits, 0, bytes copied
- *   (int64)}, zero-initialised with owner = -1.
+ *   -1 free); stamp int64 [n_slots]; state int32 [8] = {hand, 0, status bits, 0, bytes copied (int64),
+ *   plan counter (int64)}, zero-initialised with owner = -1. Stamps and the counter are 64-bit so that
+ *   they never wrap (one exact plan per layer per step).
  * EvaPoolLayer (one per layer, an array of them in device memory): layer's n_local (<= 1024) experts;
  *   host_records: pinned host memory, n_local records of record_bytes; row_off: byte offsets of the 9
  *   tensors inside a record (handle row order); slot_of [n_local] (-1 = not resident); last_needed:
@@ -321,7 +322,7 @@ typedef struct {
     int64_t record_bytes;
     void* slots;
     int32_t* owner;
-    int32_t* stamp;
+    int64_t* stamp;
     int32_t* state;
 } EvaExpertPool;
 

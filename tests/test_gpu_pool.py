@@ -75,13 +75,18 @@ class PoolModel:
         return jobs
 
 
-def test_planner_matches_policy_model_and_copies_records():
+@pytest.mark.parametrize("start", [0, 2**31 - 20], ids=["counter-0", "counter-past-int32"])
+def test_planner_matches_policy_model_and_copies_records(start):
+    """start: the plan counter the pool begins at. From 2^31 - 20 the run's plans take it past the
+    int32 range (as hours of serving would), and stamp ordering must still hold."""
     L, n_slots = 3, 20
     hosts = [make_layer(SMALL, "cpu", seed=40 + i) for i in range(L)]
     rec = hosts[0].record_bytes
     pool = ExpertPool(DEV, n_slots, rec)
+    pool.state[6:8].view(torch.int64).fill_(start)
     pls = [pool.add_layer(h) for h in hosts]
     model = PoolModel(n_slots, L, SMALL.n_experts)
+    model.counter = start
     offs, _, _ = record_layout(SMALL.hidden, SMALL.inter, SMALL.bits)
     rng = np.random.default_rng(0)
     for step in range(12):
@@ -106,8 +111,7 @@ def test_planner_matches_policy_model_and_copies_records():
             assert pool.status() == 0
             assert pool.owner.cpu().tolist() == model.owner
             assert pool.stamp.cpu().tolist() == model.stamp
-            st = pool.state.cpu().tolist()
-            assert st[0] == model.hand and st[1] == model.counter
+            assert pool.state[0].item() == model.hand and pool.plan_counter() == model.counter
             assert [(int(a), int(b)) for a, b in zip(pls[li].jobs[1::2].cpu()[: len(jobs)],
                                                      pls[li].jobs[2::2].cpu()[: len(jobs)])] == jobs
             for lj in range(L):
