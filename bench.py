@@ -638,6 +638,7 @@ def _e2e_pipelined(fwd, xh, out_shape, dev, warmup, steps):
     ev_read = [torch.cuda.Event() for _ in range(2)]
 
     def run(first, n):
+        cs.wait_stream(stream)                         # the first copy starts after the start event
         with torch.cuda.stream(cs):
             xd[0].copy_(xh[first], non_blocking=True)
             ev_in[0].record(cs)
