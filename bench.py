@@ -20,9 +20,12 @@ cpu_baseline  the CPU port of the path (FP32 numpy router + oracle/cpu_fast.c: f
 
 N > 1 (torchrun): expert parallelism. Each rank holds n_experts / N experts (placed by expected
 load) and its own batch of --batch tokens (weak scaling; global batch N * batch); a step is
-EPMoE.forward (route, dispatch, NCCL exchange of rows, shared + local experts, exchange of partial
-sums back, combine). value = all ranks' tokens / max over ranks of the timed region. The prefill
-leg runs --prefill-tokens tokens per rank the same way with exact splits.
+EPMoE.forward: route, dispatch (each token's row stored into its experts' owners' arenas over NVLink
+by this library's peer-memory kernels; --ep-transport nccl: NCCL send/recv instead), shared + local
+experts, combine (partial sums read back from the peers). value = all ranks' tokens / max over ranks
+of the timed region; phase_ms_per_step splits the step by phase (max / min over ranks) and
+placement_balance gives the routed slots and distinct experts per rank. The prefill leg runs
+--prefill-tokens tokens per rank the same way with exact splits.
 
 --impl reference: the same CPU port of the path on the host cores, one whole batch step per step,
 rank 0 only.
@@ -455,8 +458,8 @@ def _placement_balance(allidx, owner, world):
 
 def ep_bench(args, cfg, dev, rank, world, local):
     """N > 1: expert parallelism. Each rank holds n_experts / N experts (placed by expected load) and
-    its own batch of tokens (weak scaling); the step is EPMoE.forward: route, dispatch, NCCL
-    exchange, shared + local experts, exchange back, combine."""
+    its own batch of tokens (weak scaling); the step is EPMoE.forward: route, dispatch (peer-memory
+    stores, or NCCL with --ep-transport nccl), shared + local experts, combine."""
     import dataclasses
     import numpy as np
     import torch
