@@ -111,6 +111,26 @@ def test_c_abi_exports_every_declared_symbol():
     assert L.eva_exl3_dequant(None, 16, 16, 3, None, None) == _lib.EVA_ERR_INVALID
 
 
+def test_ctypes_bindings_match_the_header_prototypes():
+    """Every binding that declares argtypes passes as many arguments as the header's prototype takes:
+    a parameter added to or removed from include/eva_moe.h without the binding fails here, on CPU."""
+    from eva_b200 import _lib
+    L = _lib.load()
+    header = re.sub(r"/\*.*?\*/", "", (ROOT / "include" / "eva_moe.h").read_text(), flags=re.S)
+    protos = dict(re.findall(r"\b(eva_[a-z0-9_]+)\s*\(([^()]*)\)\s*;", header))
+    assert set(protos) == set(_lib.EXPORTS)
+    checked = 0
+    for name, params in protos.items():
+        argtypes = getattr(L, name).argtypes
+        if argtypes is None:
+            continue
+        params = params.strip()
+        n = 0 if params in ("", "void") else params.count(",") + 1
+        assert len(argtypes) == n, f"{name}: header takes {n} arguments, the binding passes {len(argtypes)}"
+        checked += 1
+    assert checked >= 20, checked
+
+
 def test_library_has_no_torch_dependency():
     import subprocess
     out = subprocess.run(["ldd", str(ROOT / "eva_b200" / "libeva_moe.so")], capture_output=True, text=True).stdout
