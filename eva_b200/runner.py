@@ -179,7 +179,11 @@ class EvaMoERunner:
 
 
 class EvaMoE:
-    """MoE-layer operator: router + routed EXL3 experts + shared expert (Block.route/Block.experts)."""
+    """MoE-layer operator: router + routed EXL3 experts + shared expert (Block.route/Block.experts).
+
+    forward(x, out=...) issues only stream-ordered work and never synchronises the host, so it can be
+    captured in a CUDA graph (torch.cuda.graph) and replayed with new inputs copied into the captured
+    x; the workspace is the operator's own, so one captured graph per operator runs at a time."""
 
     def __init__(self, layer: ExpertLayer, max_rows: int = 64):
         if not torch.cuda.is_available() or layer.device.type != "cuda":
