@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--small", action="store_true", help="small case for ncu captures (64 experts)")
     ap.add_argument("--prefill-tokens", type=int, default=4096)
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="N = 1 decode: also time the same steps replayed from CUDA graphs (one per batch)")
     ap.add_argument("--prefill-only", action="store_true")
     ap.add_argument("--stack", action="store_true",
                     help="config 5: decode stream through --stack-layers MoE layers (RMSNorm + residual, "
@@ -673,6 +675,38 @@ def _e2e_pipelined(fwd, xh, out_shape, dev, warmup, steps):
     return e0.elapsed_time(e1)
 
 
+def _graph_replay_ms(launch, stream, nb, warmup, steps):
+    """ms per step of the decode step replayed from CUDA graphs: launch(i, s) queues batch i's step
+    on stream s; one graph is captured per batch, then batches warmup .. warmup + steps - 1 are
+    replayed back to back on `stream` between two events (the eager timed region's batches)."""
+    import torch
+    side = torch.cuda.Stream(stream.device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        launch(0, side)                    # once outside capture
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    graphs = []
+    for i in range(nb):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launch(i, torch.cuda.current_stream(stream.device))
+        graphs.append(g)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            graphs[i].replay()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(steps):
+            graphs[warmup + i].replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del graphs
+    return ms
+
+
 def _dma_h2d_gbs(dev, nbytes=256 << 20):
     """Pinned host -> device rate of one cudaMemcpyAsync (the copy engine), for context beside the
     cache's device-side copy kernel."""
@@ -1073,6 +1107,17 @@ def main():
     st = moe.status()
 
     # ---- end to end through the public API with host buffers --------------------------------
+    graph_ms = None
+    if args.graph and world == 1:
+        def launch(i, s):
+            _lib.check(lib.eva_moe_route(ctypes.byref(shape), xs[i].data_ptr(), 1, M, layer.router_w.data_ptr(),
+                                         layer.router_b.data_ptr(), None, idx_all[i].data_ptr(), w_all[i].data_ptr(),
+                                         ws.data_ptr(), ws.numel(), s.cuda_stream), "route")
+            _lib.check(lib.eva_moe_experts(ctypes.byref(shape), xs[i].data_ptr(), 1, M, idx_all[i].data_ptr(), 0,
+                                           w_all[i].data_ptr(), tables, shared, ws.data_ptr(), ws.numel(), None,
+                                           out.data_ptr(), s.cuda_stream), "experts")
+        graph_ms = _graph_replay_ms(launch, stream, nb, warmup, steps)
+
     xh = xs.cpu().pin_memory()
     if world > 1:
         dist.barrier()
@@ -1157,6 +1202,10 @@ def main():
                       "ms_per_step": settle_ms / max(settle_steps, 1),
                       "note": "the settle steps before the timed region, timed as one block (>= 1 s)"},
         "device_status": st,
+        **({"graph": {"value": M / (graph_ms * 1e-3), "unit": UNIT, "ms_per_step": graph_ms,
+                      "note": "the timed steps' batches replayed from CUDA graphs (one captured per batch: "
+                              "router, top-k, permutation, experts), device-timed; value above is eager "
+                              "launches"}} if graph_ms is not None else {}),
         "prefill": prefill,
     }
     if rank == 0:
