@@ -144,7 +144,12 @@ int eva_moe_experts_window(const EvaMoeShape* shape, const void* x, int32_t x_is
                            int32_t shared_row0, int32_t shared_rows, void* workspace, size_t workspace_bytes,
                            float* out_f32, void* out_bf16, void* stream);
 
-/* Whole layer: eva_moe_route + eva_moe_experts. idx_out / w_out / logits_out may be NULL. */
+/* Whole layer: eva_moe_route + eva_moe_experts. idx_out / w_out / logits_out may be NULL.
+ * eva_moe_route, eva_moe_experts(_decode/_prefill/_window) and eva_moe_forward only queue work on
+ * `stream` (no host synchronisation, no allocation), so they can be captured in a CUDA graph and the
+ * graph replayed with new data at the captured addresses; calls that share a workspace must not run
+ * concurrently, captured or not. (The reference's binding refuses capture,
+ * runtime/ds41/csrc/moe_coop2048/binding.cu:83-85.) */
 int eva_moe_forward(const EvaMoeShape* shape, const void* x, int32_t x_is_bf16, int32_t M,
                     const float* router_w, const float* router_b,
                     const int64_t* const* tables, const int64_t* shared,
